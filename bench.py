@@ -1,0 +1,432 @@
+"""Benchmark of the B200 VCSR SpMM engine.
+
+`python bench.py --gpus N --steps K --warmup W` prints one JSON line.  A step
+is one C = A*B over the workload's matrix with inputs resident in HBM; L2 is
+flushed (256 MB write) before every timed step and each step is timed with
+CUDA events on the launching stream.  Under torchrun each rank owns one GPU;
+the reported time is the max over ranks.
+
+Workloads (synthetic stand-ins with the benchmark configurations' shapes):
+  fem (default)  62,451 x 62,451 FEM-style banded, ~4.0M nnz, O = 128.  With
+                 N GPUs every rank owns one such row panel (global A has
+                 N*62,451 rows), B is broadcast once from rank 0 over NCCL:
+                 weak scaling.
+  fem_o32 / fem_o512, uniform (O=32), powerlaw_o8 / powerlaw_o64,
+  blockdense (O=512): single-panel variants (weak scaling under N GPUs).
+  rmat           2^22 R-MAT, O = 256: A cut into N nnz-balanced row panels,
+                 B broadcast once: strong scaling.
+
+`--impl reference` times the reference's CSR algorithm (src/kernels.cu:15-33,
+restated in oracle/oracle.c) on the host cores instead, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "vcsr-spmm_b200"))
+
+METRIC = "SpMM GFLOP/s (2*nnz*O/t)"
+
+WORKLOADS = {
+    # name: (generator config, size_param, O, scaling, label)
+    "fem": ("fem", 0, 128, "weak", "fem_banded_62451_O128"),
+    "fem_o32": ("fem", 0, 32, "weak", "fem_banded_62451_O32"),
+    "fem_o512": ("fem", 0, 512, "weak", "fem_banded_62451_O512"),
+    "uniform": ("uniform", 0, 32, "weak", "uniform_4096_16pr_O32"),
+    "powerlaw_o8": ("powerlaw", 0, 8, "weak", "powerlaw_321821_O8"),
+    "powerlaw_o64": ("powerlaw", 0, 64, "weak", "powerlaw_321821_O64"),
+    "blockdense": ("blockdense", 0, 512, "weak", "blockdense_65536_O512_fp32"),
+    "rmat": ("rmat", 22, 256, "strong", "rmat_s22_O256"),
+}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="fem")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-peers", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="CPU baseline sample length")
+    return ap.parse_args()
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profile_traffic(label):
+    """DRAM bytes per launch from the committed ncu summary of this workload
+    (profiles/*.md with a line `dram_bytes_per_launch[<label>] = <n>`)."""
+    d = os.path.join(ROOT, "profiles")
+    if not os.path.isdir(d):
+        return None
+    pat = re.compile(r"dram_bytes_per_launch\[" + re.escape(label) + r"\]\s*=\s*([0-9.eE+]+)")
+    for fn in sorted(os.listdir(d)):
+        if fn.endswith((".md", ".txt")):
+            m = pat.search(open(os.path.join(d, fn)).read())
+            if m:
+                return float(m.group(1))
+    return None
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id):
+        self.index = gpu_id  # UUID (survives CUDA_VISIBLE_DEVICES remapping)
+        self.proc = None
+        self.path = f"/tmp/vcsr_clocks_{os.getpid()}.csv"
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
+                 "sw_power_cap"]
+        try:
+            for line in open(self.path):
+                f = [x.strip() for x in line.split(",")]
+                if len(f) < 9:
+                    continue
+                try:
+                    sm.append(float(f[1]))
+                    mx = float(f[2])
+                except ValueError:
+                    continue
+                for n, v in zip(names, f[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(n)
+            os.unlink(self.path)
+        except OSError:
+            return None
+        if not sm:
+            return None
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def algorithmic_bytes(csr, O):
+    touched = int(np.count_nonzero(np.bincount(csr.col, minlength=csr.N))) if csr.nnz else 0
+    return 8 * csr.nnz + 4 * (csr.M + 1) + 4 * O * touched + 4 * O * csr.M, touched
+
+
+def cpu_reference(csr, B, seconds, min_reps=3):
+    """The reference CSR algorithm on all host cores (oracle port)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    threads = oracle.max_threads()
+    M = csr.M
+    flops_full = 2.0 * csr.nnz * B.shape[1]
+    # bounded sample: leading rows holding at most ~2 GFLOP per repetition
+    rows = M
+    if flops_full > 2e9:
+        target = int(2e9 / (2.0 * B.shape[1]))
+        rows = int(np.searchsorted(csr.row_ptr, target))
+        rows = max(1, min(M, rows))
+    nnz_s = int(csr.row_ptr[rows])
+    Cm = np.empty((rows, B.shape[1]), np.float32)
+    rp, cc, vv = csr.row_ptr, csr.col, csr.val
+    oracle.csr_spmm_f32_into(rows, rp, cc, vv, B, Cm, threads)  # warm-up
+    reps, t0 = 0, time.perf_counter()
+    while reps < min_reps or time.perf_counter() - t0 < seconds:
+        oracle.csr_spmm_f32_into(rows, rp, cc, vv, B, Cm, threads)
+        reps += 1
+    dt = (time.perf_counter() - t0) / reps
+    gflops = 2.0 * nnz_s * B.shape[1] / dt / 1e9
+    sample = (f"rows [0,{rows}) of {M} ({nnz_s} of {csr.nnz} nnz), O={B.shape[1]}, "
+              f"{reps} reps x {dt * 1e3:.2f} ms")
+    return {"value": round(gflops, 3), "unit": "GFLOP/s", "cores": threads,
+            "kind": "port", "sample": sample}
+
+
+def build_inputs(args, rank, world):
+    import vcsr_b200 as V
+    cfg, size, O, scaling, label = WORKLOADS[args.workload]
+    full = V.gen_csr(cfg, args.seed + (rank if scaling == "weak" else 0), size)
+    if scaling == "strong" and world > 1:
+        cuts = V.partition_rows(full.row_ptr, world, 16)
+        csr = V.csr_row_panel(full, int(cuts[rank]), int(cuts[rank + 1]))
+        global_nnz = full.nnz
+    else:
+        csr = full
+        global_nnz = full.nnz * world
+    return csr, O, scaling, label, global_nnz
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import vcsr_b200 as V
+    cfg, size, O, scaling, label = WORKLOADS[args.workload]
+    csr = V.gen_csr(cfg, args.seed, size)
+    B = V.gen_dense_host(csr.N, O, args.seed + 1000, 0.0 if cfg == "rmat" else -1.0, 1.0)
+    per_step = max(1.0, args.cpu_seconds / max(1, args.steps))
+    for _ in range(args.warmup):
+        cpu_reference(csr, B, 0.0, min_reps=1)
+    vals = []
+    info = None
+    for _ in range(args.steps):
+        info = cpu_reference(csr, B, per_step, min_reps=1)
+        vals.append(info["value"])
+    v = float(np.median(vals))
+    flops = 2.0 * csr.nnz * O
+    line = {"metric": METRIC, "value": round(v, 3), "unit": "GFLOP/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(flops / (v * 1e9) * 1e3, 4),
+            "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "config": {"workload": label, "nnz": csr.nnz, "O": O,
+                       "algorithm": "reference CSR SpMM (src/kernels.cu:15-33) "
+                                    "on host cores, OpenMP over rows"},
+            "cpu_baseline": dict(info, value=round(v, 3)),
+            "e2e": {"value": round(v, 3), "unit": "GFLOP/s",
+                    "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    import vcsr_b200 as V
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA GPU (no CPU fallback)")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=dev)
+    stream = torch.cuda.current_stream()
+
+    csr, O, scaling, label, global_nnz = build_inputs(args, rank, world)
+    lo = 0.0 if WORKLOADS[args.workload][0] == "rmat" else -1.0
+    plan = V.Plan(csr, segw=4, bundle=32, max_O=max(O, 512))
+    info = plan.info()
+
+    # B: filled on rank 0, replicated by one NCCL broadcast (timed apart)
+    dB = torch.empty(csr.N, O, device=dev)
+    bcast_ms = None
+    if rank == 0 or world == 1:
+        V.gen_dense_device(dB, args.seed + 1000, lo, 1.0)
+    if world > 1:
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        dist.broadcast(dB, src=0)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1)], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        bcast_ms = float(t.item())
+    dC = torch.empty(csr.M, O, device=dev)
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)  # 256 MB
+
+    def step():
+        plan.spmm(dB, dC, stream=stream)
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    try:
+        uuid = str(torch.cuda.get_device_properties(dev).uuid)
+        gpu_id = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+    except Exception:
+        gpu_id = str(local)
+    clocks = Clocks(gpu_id)
+    clocks.start()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    launches = 0
+    for i in range(args.steps):
+        flush.zero_()
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+        launches += plan.last_launches
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    per = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    t_ms = torch.tensor([sum(per)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t_ms, op=dist.ReduceOp.MAX)
+    total_ms = float(t_ms.item())
+    ms_step = total_ms / args.steps
+    flops_step = 2.0 * global_nnz * O if scaling == "weak" else 2.0 * global_nnz * O
+    value = flops_step / (ms_step * 1e-3) / 1e9
+
+    # roofline of the dominant (only) kernel, per launch, on this rank
+    abytes, touched = algorithmic_bytes(csr, O)
+    avg_ms = float(np.mean(per))
+    achieved = abytes / (avg_ms * 1e-3) / 1e9
+    peak, peak_kind = peaks()
+    traffic = profile_traffic(label) if world == 1 else None
+
+    # end to end through the host-buffer entry point (pinned buffers)
+    e2e = None
+    if not args.no_e2e:
+        hB = torch.empty(csr.N, O, dtype=torch.float32, pin_memory=True)
+        hB.copy_(dB.cpu())
+        hC = torch.empty(csr.M, O, dtype=torch.float32, pin_memory=True)
+        for _ in range(max(1, min(3, args.warmup))):
+            plan.spmm_host(hB.numpy(), hC.numpy(), stream=stream)
+        if world > 1:
+            dist.barrier()
+        n_e2e = max(3, min(args.steps, 10))
+        t0 = time.perf_counter()
+        for _ in range(n_e2e):
+            plan.spmm_host(hB.numpy(), hC.numpy(), stream=stream)
+        dt = torch.tensor([(time.perf_counter() - t0) / n_e2e], device=dev,
+                          dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(dt, op=dist.ReduceOp.MAX)
+        e2e = {"value": round(flops_step / float(dt.item()) / 1e9, 3), "unit": "GFLOP/s",
+               "h2d_bytes_per_step": int(csr.N * O * 4 * world),
+               "d2h_bytes_per_step": int(csr.M * O * 4 * world),
+               "ms_per_step": round(float(dt.item()) * 1e3, 4),
+               "api": "vcsr_spmm_host (pinned host B and C)"}
+
+    peers = None
+    if not args.no_peers and world == 1:
+        peers = {}
+        d = V.DeviceCSR(csr)
+        dCp = torch.empty_like(dC)
+        best = None
+        for alg in (0, 1, 2, 3):
+            try:
+                h = V.CuSparse(d, dB, O, dCp, alg=alg)
+            except V.VcsrError:
+                continue
+            for _ in range(3):
+                flush.zero_()
+                h.run()
+            ts = []
+            for _ in range(max(5, min(args.steps, 20))):
+                flush.zero_()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                h.run()
+                b.record(stream)
+                torch.cuda.synchronize()
+                ts.append(a.elapsed_time(b))
+            h.close()
+            g = flops_step / (np.mean(ts) * 1e-3) / 1e9
+            if best is None or g > best[1]:
+                best = (V.CuSparse.ALGS[alg], g)
+        if best:
+            peers["cusparse_best"] = {"alg": best[0], "gflops": round(best[1], 2),
+                                      "ours_over_cusparse": round(value / best[1], 3)}
+        ts = []
+        for _ in range(max(5, min(args.steps, 20))):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            V.run_csr_spmm_gpu(csr.M, d.row_ptr, d.col, d.val, dB, O, dCp, stream)
+            b.record(stream)
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b))
+        peers["csr_rowwise_gflops"] = round(flops_step / (np.mean(ts) * 1e-3) / 1e9, 2)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        B = dB.cpu().numpy()
+        cpu = cpu_reference(csr, B, args.cpu_seconds)
+
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": "GFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 5), "higher_is_better": True,
+            "scaling": scaling, "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": label, "M": csr.M, "N": csr.N, "nnz": csr.nnz,
+                       "global_nnz": global_nnz, "O": O, "segw": 4, "bundle": 32,
+                       "vec_rows": info["vec_rows"], "units": info["num_units"],
+                       "split_units": info["num_split_units"],
+                       "cols_touched": touched,
+                       "l2": "flushed before every timed step (256 MB write)",
+                       "parallelism": (f"row panels x{world}, B broadcast once"
+                                       if world > 1 else "1 GPU")},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1),
+                         "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "peak_kind": peak_kind,
+                         "algorithmic_bytes": int(abytes),
+                         "kernel_ms": round(avg_ms, 5)},
+            "gpu_launches": int(launches),
+            "e2e": e2e, "clocks": clk, "cpu_baseline": cpu, "peers": peers,
+            "build_ms": round(info["build_ms"], 1),
+        }
+        if bcast_ms is not None:
+            line["bcast_ms"] = round(bcast_ms, 4)
+            line["bcast_bytes"] = int(csr.N * O * 4)
+        print(json.dumps(line), flush=True)
+    del plan
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,252 @@
+/*
+ * vcsr_spmm.h — C ABI of the B200 (sm_100a) VCSR SpMM engine.
+ *
+ * One job: C[M x O] = A[M x N, sparse] * B[N x O, dense row-major], FP32.
+ *
+ * Every entry point is extern "C", takes plain pointers and sizes and returns a
+ * vcsr_status.  No entry point exits the process; on failure the thread-local
+ * message behind vcsr_last_error() says what went wrong.  All device work is
+ * enqueued on the caller's stream (a cudaStream_t passed as void*, NULL = the
+ * legacy default stream) with no implicit device synchronisation, except where
+ * an entry point says it synchronises.
+ *
+ * Reference interfaces each group replaces are cited as file:line inside the
+ * MuuSeoTia/VCSR-SPMM tree.
+ */
+#ifndef VCSR_SPMM_H
+#define VCSR_SPMM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VCSR_ABI_VERSION 1
+
+typedef void *vcsr_stream_t; /* a cudaStream_t */
+
+typedef enum vcsr_status {
+  VCSR_OK = 0,
+  VCSR_ERR_INVALID = 1,     /* bad argument / malformed input */
+  VCSR_ERR_CUDA = 2,        /* a CUDA runtime/driver call failed */
+  VCSR_ERR_ALLOC = 3,       /* host or device allocation failed */
+  VCSR_ERR_IO = 4,          /* file could not be opened / parsed */
+  VCSR_ERR_UNSUPPORTED = 5, /* valid request this build cannot serve */
+  VCSR_ERR_NCCL = 6,        /* an NCCL call failed */
+  VCSR_ERR_TIMEOUT = 7,     /* a bounded wait ran out */
+  VCSR_ERR_RANGE = 8        /* index out of range (e.g. COO row >= M) */
+} vcsr_status;
+
+/* Where a structure's arrays live. */
+#define VCSR_HOST 0
+#define VCSR_DEVICE 1
+
+/* ------------------------------------------------------------------ errors */
+
+/* Thread-local text of the last failure (never NULL; "" when none). */
+const char *vcsr_last_error(void);
+const char *vcsr_status_string(vcsr_status s);
+int vcsr_abi_version(void);
+
+/* ------------------------------------------------------- matrix containers */
+
+/* COO triplets; replaces struct COO (include/mmio.hpp:15-19). */
+typedef struct vcsr_coo {
+  int M, N;
+  int nnz;
+  int *rows; /* 0-based */
+  int *cols; /* 0-based */
+  float *vals;
+} vcsr_coo;
+
+/* CSR; replaces struct CSR (include/csr.hpp:8-13).  row_ptr has M+1 entries. */
+typedef struct vcsr_csr {
+  int M, N, nnz;
+  int *row_ptr;
+  int *col;
+  float *val;
+} vcsr_csr;
+
+/* Segment-major VCSR; field for field struct VCSRSpMM (include/vcsr.hpp:12-23).
+ * num_groups = G, num_slots = P = group_ptr[G].  group_rows has G*bundle
+ * entries (-1 pads lanes past row M-1), lcol/val have P entries (lcol -1 and
+ * val 0 mark padding slots).  Slot of (group g, depth d, lane l) is
+ * group_ptr[g] + d*bundle + l.  segment_group_start (S+1 entries, S =
+ * ceil(N/segw)) gives the first group of each column segment (the
+ * VCSRSeg::segment_group_start of src/vcsr_seg.cu:21,53,109). */
+typedef struct vcsr_vcsr {
+  int M, N, segw, bundle;
+  int num_groups;
+  int num_segments;
+  int64_t num_slots;
+  int *group_ptr;
+  int *group_depth;
+  int *group_seg_base;
+  int *group_rows;
+  int *lcol;
+  float *val;
+  int *segment_group_start;
+} vcsr_vcsr;
+
+void vcsr_coo_free(vcsr_coo *coo);          /* host arrays from this library */
+void vcsr_csr_free(vcsr_csr *csr, int where);
+void vcsr_vcsr_free(vcsr_vcsr *v, int where);
+
+/* --------------------------------------------------------- host-side input */
+
+/* Matrix Market reader; replaces read_matrix_market_coo (include/mmio.hpp:22-45).
+ * Same semantics: '%' lines and empty lines before the size line are skipped,
+ * the size line gives M N nnz, then nnz "r c v" triples follow as
+ * whitespace-separated tokens; indices are 1-based unless the first triple has
+ * a 0 row or column; values are read as double and stored as float; no
+ * symmetric expansion; duplicates kept.  Errors: VCSR_ERR_IO for an unopenable
+ * file, a missing size line or a short/garbled data section. */
+vcsr_status vcsr_read_mtx(const char *path, vcsr_coo *out);
+
+/* COO -> CSR; replaces coo_to_csr (include/csr.hpp:16-37).  Rows are placed by
+ * a stable counting sort, then each row's entries are ordered by column; equal
+ * columns keep input order.  A row index outside [0,M) is VCSR_ERR_RANGE like
+ * the reference's "row idx out of range"; a column outside [0,N) is also
+ * rejected (the reference leaves it unchecked). */
+vcsr_status vcsr_coo_to_csr(const vcsr_coo *coo, vcsr_csr *out);
+
+/* Deterministic synthetic matrices (host, multi-threaded).  config is one of
+ * "uniform", "fem", "powerlaw", "rmat", "blockdense"; size_param overrides the
+ * config's row count (0 = the configured size; for "rmat" it is the scale,
+ * log2 of the row count).  The same (config, seed, size_param) always gives
+ * the same CSR, bit for bit. */
+vcsr_status vcsr_gen_csr(const char *config, uint64_t seed, int size_param,
+                         vcsr_csr *out);
+
+/* Fill a rows x cols row-major matrix (leading dimension ld) with values
+ * lo + (hi-lo)*u, u a 24-bit uniform drawn from (seed, element index).  Host
+ * and device fills give identical bits.  where = VCSR_HOST | VCSR_DEVICE. */
+vcsr_status vcsr_gen_dense(float *out, int64_t rows, int64_t cols, int64_t ld,
+                           uint64_t seed, float lo, float hi, int where,
+                           vcsr_stream_t stream);
+
+/* Copy a CSR between host and device (dst arrays allocated by the library). */
+vcsr_status vcsr_csr_to_device(const vcsr_csr *host, vcsr_csr *dev,
+                               vcsr_stream_t stream);
+
+/* ------------------------------------------------ VCSR format construction */
+
+/* Build the segment-major VCSR of a device-resident CSR on the GPU (segmented
+ * scan, stable radix sort, pack); replaces csr_to_vcsr_spmm
+ * (include/vcsr.hpp:25-109).  Output arrays are device allocations owned by
+ * *out (free with vcsr_vcsr_free(out, VCSR_DEVICE)).  Rows inside a segment
+ * are ordered by per-segment count descending and, on ties, by row ascending
+ * (the reference's std::sort leaves tie order unspecified). Synchronises the
+ * stream once to size the outputs. */
+vcsr_status vcsr_build_vcsr(const vcsr_csr *dev_csr, int segw, int bundle,
+                            vcsr_vcsr *out, vcsr_stream_t stream);
+
+/* Copy a device VCSR to host arrays (allocated by the library). */
+vcsr_status vcsr_vcsr_to_host(const vcsr_vcsr *dev, vcsr_vcsr *host);
+
+/* ------------------------------------------------------------- SpMM plans */
+
+typedef struct vcsr_plan vcsr_plan;
+
+#define VCSR_PLAN_REFERENCE_FORMAT 1 /* also keep the segment-major VCSR */
+
+typedef struct vcsr_plan_params {
+  int segw;     /* column segment width (--segw) */
+  int bundle;   /* rows per VCSR group (--bundle) */
+  int tileK;    /* O columns per tile (--tileK); 0 = choose per call */
+  int max_O;    /* largest O the plan will serve; sizes split-row scratch */
+  int vec_rows; /* rows per panel vector: 0 = choose from the pattern,
+                   else 1, 2, 4, 8 or 16 */
+  int chunk;    /* max union columns per work unit; 0 = choose */
+  int flags;    /* VCSR_PLAN_* */
+} vcsr_plan_params;
+
+typedef struct vcsr_plan_info {
+  int M, N, nnz;
+  int vec_rows;       /* chosen rows per panel vector */
+  int num_vectors;    /* ceil(M / vec_rows) */
+  int64_t num_union;  /* union columns over all vectors */
+  int num_units;      /* nnz-balanced work units */
+  int num_split_vectors;
+  int num_split_units;
+  int64_t panel_bytes; /* device bytes of the panel layout */
+  int has_reference_format;
+  double build_ms;    /* wall time of vcsr_plan_create */
+} vcsr_plan_info;
+
+void vcsr_plan_params_default(vcsr_plan_params *p);
+
+/* Build a plan for A.  csr_where = VCSR_HOST or VCSR_DEVICE.  The plan owns
+ * every device array it needs; the caller's CSR may be freed afterwards.
+ * Replaces the format build + upload half of run_vcsr_spmm_gpu
+ * (src/kernels.cu:120-151), done once instead of per call. */
+vcsr_status vcsr_plan_create(const vcsr_csr *csr, int csr_where,
+                             const vcsr_plan_params *params, vcsr_plan **out,
+                             vcsr_stream_t stream);
+vcsr_status vcsr_plan_get_info(const vcsr_plan *plan, vcsr_plan_info *info);
+/* Host copy of the plan's segment-major VCSR (needs VCSR_PLAN_REFERENCE_FORMAT). */
+vcsr_status vcsr_plan_export(const vcsr_plan *plan, vcsr_vcsr *host_out);
+void vcsr_plan_destroy(vcsr_plan *plan);
+
+/* C = A * B (C written, not accumulated: beta = 0 semantics, the zeroing the
+ * reference does with cudaMemset is fused).  B is N x O with leading dimension
+ * ldb >= O, C is M x O with ldc >= O, both device pointers.  Replaces the
+ * launch half of run_vcsr_spmm_gpu (src/kernels.cu:153-160); timing is left to
+ * the caller.  Calls on one plan must not overlap on the GPU (split rows share
+ * the plan's scratch).  Reports the kernel launches it made through
+ * *launches when launches != NULL. */
+vcsr_status vcsr_spmm(const vcsr_plan *plan, const float *dB, int ldb,
+                      float *dC, int ldc, int O, vcsr_stream_t stream,
+                      int *launches);
+
+/* The same product with host buffers: copies hB (N x O, ld = O) to the device,
+ * runs vcsr_spmm, copies C back to hC (M x O, ld = O) and synchronises the
+ * stream.  Host buffers should be pinned for full PCIe speed. */
+vcsr_status vcsr_spmm_host(vcsr_plan *plan, const float *hB, float *hC, int O,
+                           vcsr_stream_t stream);
+
+/* ------------------------------------------------------------ peer paths */
+
+/* Race-free SpMM straight on a device VCSR; same contract as
+ * run_vcsr_spmm_gpu (src/kernels.cu:120): C += A*B (C must hold zeros, or the
+ * partial sum to add to), ld = O for B and C.  Each group keeps its rows' sums
+ * in registers over its depth and adds them to C with vector atomics. */
+vcsr_status vcsr_spmm_segmented(const vcsr_vcsr *dev, const float *dB, int O,
+                                int tileK, float *dC, vcsr_stream_t stream);
+
+/* CSR row-wise SpMM on device arrays; same contract as run_csr_spmm_gpu
+ * (src/kernels.cu:107-118): C = A*B with ld = O. */
+vcsr_status vcsr_csr_spmm(int M, const int *d_row_ptr, const int *d_col,
+                          const float *d_val, const float *dB, int O,
+                          float *dC, vcsr_stream_t stream);
+
+/* cuSPARSE SpMM with the handle, descriptors, buffer and preprocessing made
+ * once; replaces run_cusparse_spmm (src/kernels.cu:170-235).  alg: 0 =
+ * CUSPARSE_SPMM_ALG_DEFAULT, 1 = CSR_ALG1, 2 = CSR_ALG2, 3 = CSR_ALG3. */
+typedef struct vcsr_cusparse vcsr_cusparse;
+vcsr_status vcsr_cusparse_create(int M, int N, int nnz, const int *d_row_ptr,
+                                 const int *d_col, const float *d_val,
+                                 const float *dB, int O, float *dC, int alg,
+                                 vcsr_stream_t stream, vcsr_cusparse **out);
+vcsr_status vcsr_cusparse_run(vcsr_cusparse *h, vcsr_stream_t stream);
+void vcsr_cusparse_destroy(vcsr_cusparse *h);
+
+/* -------------------------------------------------------------- multi-GPU */
+
+/* nnz-balanced row panels: cuts[0] = 0, cuts[parts] = M, cut k is the row
+ * nearest to k*nnz/parts (binary search of row_ptr) rounded to a multiple of
+ * align (rows), kept non-decreasing.  Host-only. */
+vcsr_status vcsr_partition_rows(const int *row_ptr, int M, int parts,
+                                int align, int *cuts);
+
+/* Extract rows [r0, r1) of a host CSR as a new host CSR (row ids local). */
+vcsr_status vcsr_csr_row_panel(const vcsr_csr *csr, int r0, int r1,
+                               vcsr_csr *out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VCSR_SPMM_H */

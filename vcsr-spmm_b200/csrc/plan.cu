@@ -1,0 +1,375 @@
+// plan.cu — SpMM plans: build once (layout + upload), run many times.
+//
+// vcsr_plan_create is the format-build-and-upload half of run_vcsr_spmm_gpu
+// (src/kernels.cu:120-151) done once per matrix instead of per call;
+// vcsr_spmm is its launch half (src/kernels.cu:153-160) with C written
+// instead of accumulated into a caller-zeroed buffer.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cstdlib>
+#include <cstring>
+#include <vector>
+
+#include "common.h"
+#include "panel.h"
+#include "spmm_kernels.h"
+
+using vcsr::fail;
+
+struct vcsr_plan {
+  int M = 0, N = 0, nnz = 0;
+  vcsr_plan_params params{};
+  int device = 0;
+  // vector panels on the device
+  int R = 1;
+  int num_vectors = 0;
+  int64_t num_union = 0;
+  int chunk = 0;
+  int n_units = 0, n_split_units = 0, n_split_vectors = 0;
+  int *d_ucol = nullptr;
+  float *d_uval = nullptr;
+  int4 *d_units = nullptr;
+  int2 *d_parts = nullptr;
+  int2 *d_svecs = nullptr;
+  float *d_partials = nullptr;
+  int *d_counters = nullptr;
+  int pstride = 0, counter_stride = 0;
+  int64_t panel_bytes = 0;
+  // optional segment-major VCSR (include/vcsr.hpp:12-23 layout)
+  bool has_ref = false;
+  vcsr_vcsr ref{};
+  // host-buffer entry point staging
+  float *d_stage_B = nullptr, *d_stage_C = nullptr;
+  size_t stage_B = 0, stage_C = 0;
+  double build_ms = 0;
+};
+
+namespace {
+
+template <class T>
+vcsr_status upload(T **dst, const std::vector<T> &src, cudaStream_t st,
+                   int64_t *bytes) {
+  const size_t n = src.size() ? src.size() : 1;
+  VCSR_CUDA(cudaMalloc((void **)dst, sizeof(T) * n));
+  if (!src.empty())
+    VCSR_CUDA(cudaMemcpyAsync(*dst, src.data(), sizeof(T) * src.size(),
+                              cudaMemcpyHostToDevice, st));
+  if (bytes) *bytes += (int64_t)(sizeof(T) * n);
+  return VCSR_OK;
+}
+
+void release(vcsr_plan *p) {
+  cudaFree(p->d_ucol); cudaFree(p->d_uval); cudaFree(p->d_units);
+  cudaFree(p->d_parts); cudaFree(p->d_svecs); cudaFree(p->d_partials);
+  cudaFree(p->d_counters); cudaFree(p->d_stage_B); cudaFree(p->d_stage_C);
+  if (p->has_ref) vcsr_vcsr_free(&p->ref, VCSR_DEVICE);
+}
+
+vcsr::PanelDevView view(const vcsr_plan *p) {
+  vcsr::PanelDevView v;
+  v.ucol = p->d_ucol;
+  v.uval = p->d_uval;
+  v.units = p->d_units;
+  v.n_units = p->n_units;
+  v.parts = p->d_parts;
+  v.svecs = p->d_svecs;
+  v.partials = p->d_partials;
+  v.counters = p->d_counters;
+  v.pstride = p->pstride;
+  v.counter_stride = p->counter_stride;
+  v.n_split_units = p->n_split_units;
+  v.M = p->M;
+  v.R = p->R;
+  return v;
+}
+
+// Host copy of a CSR whose rows are sorted by column (stable); *owned says
+// whether the copy must be freed.
+vcsr_status host_sorted_csr(const vcsr_csr *in, int where, vcsr_csr *out,
+                            bool *owned) {
+  *owned = false;
+  vcsr_csr h = *in;
+  if (where == VCSR_DEVICE) {
+    h.row_ptr = (int *)malloc(sizeof(int) * ((size_t)in->M + 1));
+    h.col = (int *)malloc(sizeof(int) * (size_t)(in->nnz ? in->nnz : 1));
+    h.val = (float *)malloc(sizeof(float) * (size_t)(in->nnz ? in->nnz : 1));
+    *owned = true;
+    if (!h.row_ptr || !h.col || !h.val) {
+      vcsr_csr_free(&h, VCSR_HOST);
+      return fail(VCSR_ERR_ALLOC, "out of host memory");
+    }
+    VCSR_CUDA(cudaMemcpy(h.row_ptr, in->row_ptr, sizeof(int) * ((size_t)in->M + 1),
+                         cudaMemcpyDeviceToHost));
+    if (in->nnz) {
+      VCSR_CUDA(cudaMemcpy(h.col, in->col, sizeof(int) * (size_t)in->nnz,
+                           cudaMemcpyDeviceToHost));
+      VCSR_CUDA(cudaMemcpy(h.val, in->val, sizeof(float) * (size_t)in->nnz,
+                           cudaMemcpyDeviceToHost));
+    }
+  }
+  // validate
+  if (h.row_ptr[0] != 0 || h.row_ptr[h.M] != h.nnz) {
+    if (*owned) vcsr_csr_free(&h, VCSR_HOST);
+    return fail(VCSR_ERR_INVALID, "row_ptr must start at 0 and end at nnz");
+  }
+  bool sorted = true;
+  for (int r = 0; r < h.M; ++r) {
+    if (h.row_ptr[r + 1] < h.row_ptr[r]) {
+      if (*owned) vcsr_csr_free(&h, VCSR_HOST);
+      return fail(VCSR_ERR_INVALID, "row_ptr decreases at row %d", r);
+    }
+    for (int p = h.row_ptr[r]; p < h.row_ptr[r + 1]; ++p) {
+      if (h.col[p] < 0 || h.col[p] >= h.N) {
+        if (*owned) vcsr_csr_free(&h, VCSR_HOST);
+        return fail(VCSR_ERR_RANGE, "column %d of entry %d outside [0, %d)",
+                    h.col[p], p, h.N);
+      }
+      if (p > h.row_ptr[r] && h.col[p] < h.col[p - 1]) sorted = false;
+    }
+  }
+  if (!sorted) {  // stable per-row sort of a private copy
+    vcsr_csr s = h;
+    s.row_ptr = (int *)malloc(sizeof(int) * ((size_t)h.M + 1));
+    s.col = (int *)malloc(sizeof(int) * (size_t)(h.nnz ? h.nnz : 1));
+    s.val = (float *)malloc(sizeof(float) * (size_t)(h.nnz ? h.nnz : 1));
+    if (!s.row_ptr || !s.col || !s.val) {
+      vcsr_csr_free(&s, VCSR_HOST);
+      if (*owned) vcsr_csr_free(&h, VCSR_HOST);
+      return fail(VCSR_ERR_ALLOC, "out of host memory");
+    }
+    std::memcpy(s.row_ptr, h.row_ptr, sizeof(int) * ((size_t)h.M + 1));
+#pragma omp parallel for schedule(dynamic, 256)
+    for (int r = 0; r < h.M; ++r) {
+      const int b = h.row_ptr[r], e = h.row_ptr[r + 1];
+      std::vector<int> idx(e - b);
+      for (int q = 0; q < e - b; ++q) idx[q] = b + q;
+      std::stable_sort(idx.begin(), idx.end(),
+                       [&](int a, int c) { return h.col[a] < h.col[c]; });
+      for (int q = 0; q < e - b; ++q) {
+        s.col[b + q] = h.col[idx[q]];
+        s.val[b + q] = h.val[idx[q]];
+      }
+    }
+    if (*owned) vcsr_csr_free(&h, VCSR_HOST);
+    h = s;
+    *owned = true;
+  }
+  *out = h;
+  return VCSR_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+void vcsr_plan_params_default(vcsr_plan_params *p) {
+  if (!p) return;
+  p->segw = 4;
+  p->bundle = 32;
+  p->tileK = 0;
+  p->max_O = 512;
+  p->vec_rows = 0;
+  p->chunk = 0;
+  p->flags = 0;
+}
+
+vcsr_status vcsr_plan_create(const vcsr_csr *csr, int csr_where,
+                             const vcsr_plan_params *params, vcsr_plan **out,
+                             vcsr_stream_t stream) {
+  vcsr::clear_error();
+  if (!csr || !params || !out) return fail(VCSR_ERR_INVALID, "null argument");
+  *out = nullptr;
+  if (csr->M < 0 || csr->N < 0 || csr->nnz < 0)
+    return fail(VCSR_ERR_INVALID, "negative matrix size");
+  if (params->segw <= 0 || params->bundle <= 0)
+    return fail(VCSR_ERR_INVALID, "segw and bundle must be > 0");
+  if (params->max_O < 0 || params->tileK < 0)
+    return fail(VCSR_ERR_INVALID, "negative max_O or tileK");
+  if (csr->M > 0 && !csr->row_ptr) return fail(VCSR_ERR_INVALID, "null row_ptr");
+  if (csr->nnz > 0 && (!csr->col || !csr->val))
+    return fail(VCSR_ERR_INVALID, "null col/val");
+  const auto t0 = std::chrono::steady_clock::now();
+  cudaStream_t st = (cudaStream_t)stream;
+  vcsr_plan *p = new (std::nothrow) vcsr_plan();
+  if (!p) return fail(VCSR_ERR_ALLOC, "out of host memory");
+  p->M = csr->M; p->N = csr->N; p->nnz = csr->nnz;
+  p->params = *params;
+  cudaGetDevice(&p->device);
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, p->device);
+
+  vcsr_csr h{};
+  bool owned = false;
+  vcsr_csr empty_rp{};
+  std::vector<int> zero_rp;
+  if (csr->M == 0) {  // nothing to read; keep a valid row_ptr
+    zero_rp.assign(1, 0);
+    empty_rp = *csr;
+    empty_rp.row_ptr = zero_rp.data();
+    h = empty_rp;
+  } else {
+    vcsr_status s = host_sorted_csr(csr, csr_where, &h, &owned);
+    if (s != VCSR_OK) { delete p; return s; }
+  }
+
+  vcsr::PanelHost ph;
+  int R = params->vec_rows;
+  if (R == 0) R = vcsr::choose_vec_rows(h, nullptr);
+  vcsr_status s = vcsr::build_panel_host(h, R, params->chunk, sms, &ph);
+  if (s != VCSR_OK) {
+    if (owned) vcsr_csr_free(&h, VCSR_HOST);
+    delete p;
+    return s;
+  }
+  p->R = ph.R;
+  p->num_vectors = ph.num_vectors;
+  p->num_union = (int64_t)ph.ucol.size();
+  p->chunk = ph.chunk;
+  p->n_units = (int)ph.units.size();
+  p->n_split_units = (int)ph.parts.size();
+  p->n_split_vectors = (int)ph.svecs.size();
+  p->pstride = std::max(params->max_O, 1);
+  p->counter_stride = std::max(params->max_O, 1);
+  static_assert(sizeof(vcsr::Unit) == sizeof(int4), "Unit must match int4");
+  static_assert(sizeof(vcsr::SplitPart) == sizeof(int2), "SplitPart must match int2");
+  static_assert(sizeof(vcsr::SplitVec) == sizeof(int2), "SplitVec must match int2");
+  std::vector<int4> units(ph.units.size());
+  std::memcpy(units.data(), ph.units.data(), sizeof(int4) * units.size());
+  std::vector<int2> parts(ph.parts.size()), svecs(ph.svecs.size());
+  std::memcpy(parts.data(), ph.parts.data(), sizeof(int2) * parts.size());
+  std::memcpy(svecs.data(), ph.svecs.data(), sizeof(int2) * svecs.size());
+  if ((s = upload(&p->d_ucol, ph.ucol, st, &p->panel_bytes)) ||
+      (s = upload(&p->d_uval, ph.uval, st, &p->panel_bytes)) ||
+      (s = upload(&p->d_units, units, st, &p->panel_bytes)) ||
+      (s = upload(&p->d_parts, parts, st, &p->panel_bytes)) ||
+      (s = upload(&p->d_svecs, svecs, st, &p->panel_bytes))) {
+    if (owned) vcsr_csr_free(&h, VCSR_HOST);
+    release(p);
+    delete p;
+    return s;
+  }
+  if (p->n_split_units > 0) {
+    const size_t pbytes = sizeof(float) * (size_t)p->n_split_units * p->R * p->pstride;
+    const size_t cbytes = sizeof(int) * (size_t)p->n_split_vectors * p->counter_stride;
+    cudaError_t e = cudaMalloc(&p->d_partials, pbytes);
+    if (e == cudaSuccess) e = cudaMalloc(&p->d_counters, cbytes);
+    if (e == cudaSuccess) e = cudaMemsetAsync(p->d_counters, 0, cbytes, st);
+    if (e != cudaSuccess) {
+      if (owned) vcsr_csr_free(&h, VCSR_HOST);
+      release(p);
+      delete p;
+      return fail(VCSR_ERR_CUDA, "split scratch: %s", cudaGetErrorString(e));
+    }
+    p->panel_bytes += (int64_t)(pbytes + cbytes);
+  }
+  if (params->flags & VCSR_PLAN_REFERENCE_FORMAT) {
+    vcsr_csr d{};
+    s = vcsr_csr_to_device(&h, &d, stream);
+    if (s == VCSR_OK) s = vcsr_build_vcsr(&d, params->segw, params->bundle, &p->ref, stream);
+    if (d.row_ptr) {
+      cudaStreamSynchronize(st);
+      vcsr_csr_free(&d, VCSR_DEVICE);
+    }
+    if (s != VCSR_OK) {
+      if (owned) vcsr_csr_free(&h, VCSR_HOST);
+      release(p);
+      delete p;
+      return s;
+    }
+    p->has_ref = true;
+  }
+  cudaError_t e = cudaStreamSynchronize(st);  // host vectors die here
+  if (owned) vcsr_csr_free(&h, VCSR_HOST);
+  if (e != cudaSuccess) {
+    release(p);
+    delete p;
+    return fail(VCSR_ERR_CUDA, "plan upload: %s", cudaGetErrorString(e));
+  }
+  p->build_ms = std::chrono::duration<double, std::milli>(
+                    std::chrono::steady_clock::now() - t0).count();
+  *out = p;
+  return VCSR_OK;
+}
+
+vcsr_status vcsr_plan_get_info(const vcsr_plan *p, vcsr_plan_info *info) {
+  vcsr::clear_error();
+  if (!p || !info) return fail(VCSR_ERR_INVALID, "null argument");
+  info->M = p->M; info->N = p->N; info->nnz = p->nnz;
+  info->vec_rows = p->R;
+  info->num_vectors = p->num_vectors;
+  info->num_union = p->num_union;
+  info->num_units = p->n_units;
+  info->num_split_vectors = p->n_split_vectors;
+  info->num_split_units = p->n_split_units;
+  info->panel_bytes = p->panel_bytes;
+  info->has_reference_format = p->has_ref ? 1 : 0;
+  info->build_ms = p->build_ms;
+  return VCSR_OK;
+}
+
+vcsr_status vcsr_plan_export(const vcsr_plan *p, vcsr_vcsr *host_out) {
+  vcsr::clear_error();
+  if (!p || !host_out) return fail(VCSR_ERR_INVALID, "null argument");
+  if (!p->has_ref)
+    return fail(VCSR_ERR_INVALID,
+                "plan was built without VCSR_PLAN_REFERENCE_FORMAT");
+  return vcsr_vcsr_to_host(&p->ref, host_out);
+}
+
+void vcsr_plan_destroy(vcsr_plan *p) {
+  if (!p) return;
+  release(p);
+  delete p;
+}
+
+vcsr_status vcsr_spmm(const vcsr_plan *p, const float *dB, int ldb, float *dC,
+                      int ldc, int O, vcsr_stream_t stream, int *launches) {
+  vcsr::clear_error();
+  if (launches) *launches = 0;
+  if (!p) return fail(VCSR_ERR_INVALID, "null plan");
+  if (O < 0 || ldb < O || ldc < O)
+    return fail(VCSR_ERR_INVALID, "need 0 <= O <= ldb, ldc (O=%d ldb=%d ldc=%d)",
+                O, ldb, ldc);
+  if (O == 0 || p->M == 0) return VCSR_OK;
+  if (!dC || (!dB && p->N > 0)) return fail(VCSR_ERR_INVALID, "null B or C");
+  if (p->n_split_units > 0 && O > p->pstride)
+    return fail(VCSR_ERR_INVALID,
+                "O=%d exceeds the plan's max_O=%d (split rows need scratch)", O,
+                p->pstride);
+  return vcsr::launch_panel_spmm(view(p), false, dB, ldb, dC, ldc, O,
+                                 (cudaStream_t)stream, launches);
+}
+
+vcsr_status vcsr_spmm_host(vcsr_plan *p, const float *hB, float *hC, int O,
+                           vcsr_stream_t stream) {
+  vcsr::clear_error();
+  if (!p || !hC || (!hB && p->N > 0 && O > 0))
+    return fail(VCSR_ERR_INVALID, "null argument");
+  if (O < 0) return fail(VCSR_ERR_INVALID, "negative O");
+  cudaStream_t st = (cudaStream_t)stream;
+  const size_t nb = sizeof(float) * (size_t)p->N * O;
+  const size_t nc = sizeof(float) * (size_t)p->M * O;
+  if (nb > p->stage_B) {
+    cudaFree(p->d_stage_B);
+    p->d_stage_B = nullptr;
+    p->stage_B = 0;
+    VCSR_CUDA(cudaMalloc(&p->d_stage_B, nb));
+    p->stage_B = nb;
+  }
+  if (nc > p->stage_C) {
+    cudaFree(p->d_stage_C);
+    p->d_stage_C = nullptr;
+    p->stage_C = 0;
+    VCSR_CUDA(cudaMalloc(&p->d_stage_C, nc));
+    p->stage_C = nc;
+  }
+  if (nb) VCSR_CUDA(cudaMemcpyAsync(p->d_stage_B, hB, nb, cudaMemcpyHostToDevice, st));
+  VCSR_TRY(vcsr_spmm(p, p->d_stage_B, O, p->d_stage_C, O, O, stream, nullptr));
+  if (nc) VCSR_CUDA(cudaMemcpyAsync(hC, p->d_stage_C, nc, cudaMemcpyDeviceToHost, st));
+  VCSR_CUDA(cudaStreamSynchronize(st));
+  return VCSR_OK;
+}
+
+}  // extern "C"

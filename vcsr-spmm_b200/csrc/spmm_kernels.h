@@ -1,0 +1,42 @@
+// spmm_kernels.h — internal launch interface of the SpMM kernels.
+#pragma once
+#include <cuda_runtime.h>
+
+#include "common.h"
+
+namespace vcsr {
+
+// Device view of a vector-panel layout (panel.h) or, with row_ptr set and
+// R = 1, of a plain CSR (one unit per row, never split).
+struct PanelDevView {
+  const int *ucol = nullptr;
+  const float *uval = nullptr;
+  const int4 *units = nullptr;    // {vector, begin, end, split slot or -1}
+  const int *row_ptr = nullptr;   // CSR mode only
+  int n_units = 0;
+  const int2 *parts = nullptr;    // per split slot: {split vector, part}
+  const int2 *svecs = nullptr;    // per split vector: {first slot, nparts}
+  float *partials = nullptr;      // split slots x R x pstride floats
+  int *counters = nullptr;        // split vectors x counter_stride tickets
+  int pstride = 0;                // = the plan's max_O
+  int counter_stride = 0;         // >= O-tiles of any launch shape
+  int n_split_units = 0;
+  int M = 0;
+  int R = 1;
+};
+
+struct LaunchShape {
+  int VW;        // floats per access: 4 (128-bit) or 1
+  int NV;        // accesses per lane per O-tile
+  int lshift;    // log2 of lanes per sub-warp
+  int W;         // O columns per tile
+  int n_otiles;  // tiles over O
+};
+
+LaunchShape pick_shape(int O, int R, bool vec4);
+
+vcsr_status launch_panel_spmm(const PanelDevView &P, bool rowptr,
+                              const float *B, int ldb, float *C, int ldc, int O,
+                              cudaStream_t st, int *launches);
+
+}  // namespace vcsr

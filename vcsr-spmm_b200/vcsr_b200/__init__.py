@@ -1,0 +1,474 @@
+"""Python front end of the B200 VCSR SpMM engine (ctypes over the C ABI in
+include/vcsr_spmm.h, implemented by lib/libvcsr_b200.so).
+
+The names mirror the reference's C++ interface so that tests read like the
+reference's own call sites:
+
+    read_matrix_market_coo   include/mmio.hpp:22      -> vcsr_read_mtx
+    coo_to_csr               include/csr.hpp:16       -> vcsr_coo_to_csr
+    csr_to_vcsr_spmm         include/vcsr.hpp:25      -> vcsr_build_vcsr (GPU)
+    run_vcsr_spmm_gpu        src/kernels.cu:120       -> vcsr_spmm_segmented
+    run_csr_spmm_gpu         src/kernels.cu:107       -> vcsr_csr_spmm
+    run_cusparse_spmm        src/kernels.cu:170       -> CuSparse
+and Plan (vcsr_plan_*) is the engine's own build-once / run-many operator.
+
+There is no CPU fallback: if the library is missing, importing this module
+works but every call raises VcsrError.  Device buffers are torch CUDA tensors
+(or raw device pointers); streams are torch.cuda.Stream objects or raw
+cudaStream_t integers.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from dataclasses import dataclass
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.dirname(HERE)
+LIB_PATH = os.path.join(PKG, "lib", "libvcsr_b200.so")
+
+_i32p = C.POINTER(C.c_int)
+_f32p = C.POINTER(C.c_float)
+
+STATUS = {0: "ok", 1: "invalid", 2: "cuda", 3: "alloc", 4: "io",
+          5: "unsupported", 6: "nccl", 7: "timeout", 8: "range"}
+HOST, DEVICE = 0, 1
+PLAN_REFERENCE_FORMAT = 1
+
+
+class VcsrError(RuntimeError):
+    def __init__(self, status, msg):
+        super().__init__(f"{STATUS.get(status, status)}: {msg}")
+        self.status = status
+        self.msg = msg
+
+
+class _Coo(C.Structure):
+    _fields_ = [("M", C.c_int), ("N", C.c_int), ("nnz", C.c_int),
+                ("rows", _i32p), ("cols", _i32p), ("vals", _f32p)]
+
+
+class _Csr(C.Structure):
+    _fields_ = [("M", C.c_int), ("N", C.c_int), ("nnz", C.c_int),
+                ("row_ptr", C.c_void_p), ("col", C.c_void_p), ("val", C.c_void_p)]
+
+
+class _Vcsr(C.Structure):
+    _fields_ = [("M", C.c_int), ("N", C.c_int), ("segw", C.c_int),
+                ("bundle", C.c_int), ("num_groups", C.c_int),
+                ("num_segments", C.c_int), ("num_slots", C.c_int64),
+                ("group_ptr", C.c_void_p), ("group_depth", C.c_void_p),
+                ("group_seg_base", C.c_void_p), ("group_rows", C.c_void_p),
+                ("lcol", C.c_void_p), ("val", C.c_void_p),
+                ("segment_group_start", C.c_void_p)]
+
+
+class _PlanParams(C.Structure):
+    _fields_ = [("segw", C.c_int), ("bundle", C.c_int), ("tileK", C.c_int),
+                ("max_O", C.c_int), ("vec_rows", C.c_int), ("chunk", C.c_int),
+                ("flags", C.c_int)]
+
+
+class _PlanInfo(C.Structure):
+    _fields_ = [("M", C.c_int), ("N", C.c_int), ("nnz", C.c_int),
+                ("vec_rows", C.c_int), ("num_vectors", C.c_int),
+                ("num_union", C.c_int64), ("num_units", C.c_int),
+                ("num_split_vectors", C.c_int), ("num_split_units", C.c_int),
+                ("panel_bytes", C.c_int64), ("has_reference_format", C.c_int),
+                ("build_ms", C.c_double)]
+
+
+_LIB = None
+
+# every function of include/vcsr_spmm.h with its ctypes signature
+_SIGS = {
+    "vcsr_last_error": (C.c_char_p, []),
+    "vcsr_status_string": (C.c_char_p, [C.c_int]),
+    "vcsr_abi_version": (C.c_int, []),
+    "vcsr_coo_free": (None, [C.POINTER(_Coo)]),
+    "vcsr_csr_free": (None, [C.POINTER(_Csr), C.c_int]),
+    "vcsr_vcsr_free": (None, [C.POINTER(_Vcsr), C.c_int]),
+    "vcsr_read_mtx": (C.c_int, [C.c_char_p, C.POINTER(_Coo)]),
+    "vcsr_coo_to_csr": (C.c_int, [C.POINTER(_Coo), C.POINTER(_Csr)]),
+    "vcsr_gen_csr": (C.c_int, [C.c_char_p, C.c_uint64, C.c_int, C.POINTER(_Csr)]),
+    "vcsr_gen_dense": (C.c_int, [C.c_void_p, C.c_int64, C.c_int64, C.c_int64,
+                                 C.c_uint64, C.c_float, C.c_float, C.c_int,
+                                 C.c_void_p]),
+    "vcsr_csr_to_device": (C.c_int, [C.POINTER(_Csr), C.POINTER(_Csr), C.c_void_p]),
+    "vcsr_build_vcsr": (C.c_int, [C.POINTER(_Csr), C.c_int, C.c_int,
+                                  C.POINTER(_Vcsr), C.c_void_p]),
+    "vcsr_vcsr_to_host": (C.c_int, [C.POINTER(_Vcsr), C.POINTER(_Vcsr)]),
+    "vcsr_plan_params_default": (None, [C.POINTER(_PlanParams)]),
+    "vcsr_plan_create": (C.c_int, [C.POINTER(_Csr), C.c_int, C.POINTER(_PlanParams),
+                                   C.POINTER(C.c_void_p), C.c_void_p]),
+    "vcsr_plan_get_info": (C.c_int, [C.c_void_p, C.POINTER(_PlanInfo)]),
+    "vcsr_plan_export": (C.c_int, [C.c_void_p, C.POINTER(_Vcsr)]),
+    "vcsr_plan_destroy": (None, [C.c_void_p]),
+    "vcsr_spmm": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int,
+                            C.c_int, C.c_void_p, C.POINTER(C.c_int)]),
+    "vcsr_spmm_host": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+                                 C.c_void_p]),
+    "vcsr_spmm_segmented": (C.c_int, [C.POINTER(_Vcsr), C.c_void_p, C.c_int, C.c_int,
+                                      C.c_void_p, C.c_void_p]),
+    "vcsr_csr_spmm": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
+    "vcsr_cusparse_create": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_void_p,
+                                       C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+                                       C.c_void_p, C.c_int, C.c_void_p,
+                                       C.POINTER(C.c_void_p)]),
+    "vcsr_cusparse_run": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "vcsr_cusparse_destroy": (None, [C.c_void_p]),
+    "vcsr_partition_rows": (C.c_int, [_i32p, C.c_int, C.c_int, C.c_int, _i32p]),
+    "vcsr_csr_row_panel": (C.c_int, [C.POINTER(_Csr), C.c_int, C.c_int,
+                                     C.POINTER(_Csr)]),
+}
+
+
+def lib():
+    """Load the engine library (raises VcsrError if it was not built)."""
+    global _LIB
+    if _LIB is None:
+        if not os.path.exists(LIB_PATH):
+            raise VcsrError(5, f"{LIB_PATH} is missing: build it with "
+                               "`make -C vcsr-spmm_b200` (no CPU fallback)")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _LIB = L
+    return _LIB
+
+
+def exported_names():
+    return list(_SIGS)
+
+
+def _check(st):
+    if st != 0:
+        raise VcsrError(st, lib().vcsr_last_error().decode())
+
+
+def _stream(s):
+    if s is None:
+        try:
+            import torch
+            if torch.cuda.is_available():
+                return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+        except ImportError:
+            pass
+        return C.c_void_p(0)
+    if isinstance(s, int):
+        return C.c_void_p(s)
+    return C.c_void_p(s.cuda_stream)
+
+
+def _ptr(x):
+    if x is None:
+        return C.c_void_p(0)
+    if isinstance(x, int):
+        return C.c_void_p(x)
+    if isinstance(x, np.ndarray):
+        return x.ctypes.data_as(C.c_void_p)
+    return C.c_void_p(x.data_ptr())
+
+
+def _take(ptr, n, dtype):
+    if n == 0 or not ptr:
+        return np.zeros(0, dtype)
+    ct = {np.int32: C.c_int, np.float32: C.c_float}[dtype]
+    arr = C.cast(ptr, C.POINTER(ct))
+    return np.ctypeslib.as_array(arr, shape=(n,)).astype(dtype, copy=True)
+
+
+# ----------------------------------------------------------------- host data
+
+@dataclass
+class COO:
+    """struct COO (include/mmio.hpp:15-19)."""
+    M: int
+    N: int
+    rows: np.ndarray
+    cols: np.ndarray
+    vals: np.ndarray
+
+
+@dataclass
+class CSR:
+    """struct CSR (include/csr.hpp:8-13), host arrays."""
+    M: int
+    N: int
+    nnz: int
+    row_ptr: np.ndarray
+    col: np.ndarray
+    val: np.ndarray
+
+    def _struct(self):
+        self.row_ptr = np.ascontiguousarray(self.row_ptr, np.int32)
+        self.col = np.ascontiguousarray(self.col, np.int32)
+        self.val = np.ascontiguousarray(self.val, np.float32)
+        return _Csr(self.M, self.N, self.nnz, self.row_ptr.ctypes.data,
+                    self.col.ctypes.data, self.val.ctypes.data)
+
+
+@dataclass
+class VCSRSpMM:
+    """struct VCSRSpMM (include/vcsr.hpp:12-23), host arrays."""
+    M: int
+    N: int
+    segw: int
+    bundle: int
+    group_ptr: np.ndarray
+    group_depth: np.ndarray
+    group_seg_base: np.ndarray
+    group_rows: np.ndarray
+    lcol: np.ndarray
+    val: np.ndarray
+    segment_group_start: np.ndarray
+
+    @property
+    def num_groups(self):
+        return len(self.group_depth)
+
+    @property
+    def num_slots(self):
+        return len(self.lcol)
+
+    def as_dict(self):
+        return dict(M=self.M, N=self.N, segw=self.segw, bundle=self.bundle,
+                    num_groups=self.num_groups, num_slots=self.num_slots,
+                    group_ptr=self.group_ptr, group_depth=self.group_depth,
+                    group_seg_base=self.group_seg_base, group_rows=self.group_rows,
+                    lcol=self.lcol, val=self.val,
+                    segment_group_start=self.segment_group_start)
+
+
+def _csr_from_struct(s):
+    L = lib()
+    out = CSR(s.M, s.N, s.nnz, _take(s.row_ptr, s.M + 1, np.int32),
+              _take(s.col, s.nnz, np.int32), _take(s.val, s.nnz, np.float32))
+    L.vcsr_csr_free(C.byref(s), HOST)
+    return out
+
+
+def _vcsr_from_host_struct(v):
+    G, P, S, b = v.num_groups, v.num_slots, v.num_segments, v.bundle
+    out = VCSRSpMM(v.M, v.N, v.segw, b, _take(v.group_ptr, G + 1, np.int32),
+                   _take(v.group_depth, G, np.int32),
+                   _take(v.group_seg_base, G, np.int32),
+                   _take(v.group_rows, G * b, np.int32),
+                   _take(v.lcol, P, np.int32), _take(v.val, P, np.float32),
+                   _take(v.segment_group_start, S + 1, np.int32))
+    lib().vcsr_vcsr_free(C.byref(v), HOST)
+    return out
+
+
+def read_matrix_market_coo(path) -> COO:
+    """read_matrix_market_coo (include/mmio.hpp:22-45)."""
+    L = lib()
+    s = _Coo()
+    _check(L.vcsr_read_mtx(os.fsencode(path), C.byref(s)))
+    out = COO(s.M, s.N, _take(s.rows, s.nnz, np.int32),
+              _take(s.cols, s.nnz, np.int32), _take(s.vals, s.nnz, np.float32))
+    L.vcsr_coo_free(C.byref(s))
+    return out
+
+
+def coo_to_csr(coo: COO) -> CSR:
+    """coo_to_csr (include/csr.hpp:16-37)."""
+    L = lib()
+    r = np.ascontiguousarray(coo.rows, np.int32)
+    c = np.ascontiguousarray(coo.cols, np.int32)
+    v = np.ascontiguousarray(coo.vals, np.float32)
+    s = _Coo(coo.M, coo.N, len(v), r.ctypes.data_as(_i32p), c.ctypes.data_as(_i32p),
+             v.ctypes.data_as(_f32p))
+    out = _Csr()
+    _check(L.vcsr_coo_to_csr(C.byref(s), C.byref(out)))
+    return _csr_from_struct(out)
+
+
+def gen_csr(config: str, seed: int = 0, size: int = 0) -> CSR:
+    """Deterministic synthetic matrix (vcsr_gen_csr)."""
+    out = _Csr()
+    _check(lib().vcsr_gen_csr(config.encode(), seed, size, C.byref(out)))
+    return _csr_from_struct(out)
+
+
+def gen_dense_host(rows, cols, seed, lo=-1.0, hi=1.0) -> np.ndarray:
+    a = np.empty((rows, cols), np.float32)
+    _check(lib().vcsr_gen_dense(a.ctypes.data, rows, cols, cols, seed, lo, hi,
+                                HOST, None))
+    return a
+
+
+def gen_dense_device(t, seed, lo=-1.0, hi=1.0, stream=None):
+    """Fill a 2-D torch CUDA float32 tensor in place (same bits as the host)."""
+    rows, cols = t.shape
+    _check(lib().vcsr_gen_dense(_ptr(t), rows, cols, t.stride(0), seed, lo, hi,
+                                DEVICE, _stream(stream)))
+    return t
+
+
+def partition_rows(row_ptr, parts, align=1) -> np.ndarray:
+    rp = np.ascontiguousarray(row_ptr, np.int32)
+    cuts = np.zeros(parts + 1, np.int32)
+    _check(lib().vcsr_partition_rows(rp.ctypes.data_as(_i32p), len(rp) - 1, parts,
+                                     align, cuts.ctypes.data_as(_i32p)))
+    return cuts
+
+
+def csr_row_panel(csr: CSR, r0, r1) -> CSR:
+    s = csr._struct()
+    out = _Csr()
+    _check(lib().vcsr_csr_row_panel(C.byref(s), r0, r1, C.byref(out)))
+    return _csr_from_struct(out)
+
+
+# --------------------------------------------------------------- device data
+
+class DeviceCSR:
+    """A CSR whose arrays are torch CUDA tensors."""
+
+    def __init__(self, csr: CSR, device=None):
+        import torch
+        dev = device or torch.device("cuda", torch.cuda.current_device())
+        self.M, self.N, self.nnz = csr.M, csr.N, csr.nnz
+        self.row_ptr = torch.from_numpy(np.ascontiguousarray(csr.row_ptr, np.int32)).to(dev)
+        self.col = torch.from_numpy(np.ascontiguousarray(csr.col, np.int32)).to(dev)
+        self.val = torch.from_numpy(np.ascontiguousarray(csr.val, np.float32)).to(dev)
+
+    def _struct(self):
+        return _Csr(self.M, self.N, self.nnz, self.row_ptr.data_ptr(),
+                    self.col.data_ptr(), self.val.data_ptr())
+
+
+class DeviceVCSR:
+    """A segment-major VCSR with device arrays owned by the library."""
+
+    def __init__(self, s: _Vcsr):
+        self._s = s
+
+    @property
+    def num_groups(self):
+        return self._s.num_groups
+
+    @property
+    def num_slots(self):
+        return self._s.num_slots
+
+    def to_host(self) -> VCSRSpMM:
+        h = _Vcsr()
+        _check(lib().vcsr_vcsr_to_host(C.byref(self._s), C.byref(h)))
+        return _vcsr_from_host_struct(h)
+
+    def close(self):
+        if self._s is not None:
+            lib().vcsr_vcsr_free(C.byref(self._s), DEVICE)
+            self._s = None
+
+    __del__ = close
+
+
+def csr_to_vcsr_spmm(dcsr: DeviceCSR, segw=4, bundle=32, stream=None) -> DeviceVCSR:
+    """csr_to_vcsr_spmm (include/vcsr.hpp:25-109), built on the GPU."""
+    s = dcsr._struct()
+    out = _Vcsr()
+    _check(lib().vcsr_build_vcsr(C.byref(s), segw, bundle, C.byref(out),
+                                 _stream(stream)))
+    return DeviceVCSR(out)
+
+
+def run_vcsr_spmm_gpu(V: DeviceVCSR, dB, O, tileK, dC, stream=None):
+    """run_vcsr_spmm_gpu (src/kernels.cu:120): C += A*B, race-free."""
+    _check(lib().vcsr_spmm_segmented(C.byref(V._s), _ptr(dB), O, tileK, _ptr(dC),
+                                     _stream(stream)))
+
+
+def run_csr_spmm_gpu(M, d_rowptr, d_col, d_val, dB, O, dC, stream=None):
+    """run_csr_spmm_gpu (src/kernels.cu:107): C = A*B."""
+    _check(lib().vcsr_csr_spmm(M, _ptr(d_rowptr), _ptr(d_col), _ptr(d_val),
+                               _ptr(dB), O, _ptr(dC), _stream(stream)))
+
+
+class CuSparse:
+    """cuSPARSE SpMM with handle/buffer made once (src/kernels.cu:170-235)."""
+    ALGS = {0: "ALG_DEFAULT", 1: "CSR_ALG1", 2: "CSR_ALG2", 3: "CSR_ALG3"}
+
+    def __init__(self, dcsr: DeviceCSR, dB, O, dC, alg=0, stream=None):
+        h = C.c_void_p()
+        _check(lib().vcsr_cusparse_create(dcsr.M, dcsr.N, dcsr.nnz,
+                                          _ptr(dcsr.row_ptr), _ptr(dcsr.col),
+                                          _ptr(dcsr.val), _ptr(dB), O, _ptr(dC),
+                                          alg, _stream(stream), C.byref(h)))
+        self._h = h
+        self.alg = alg
+
+    def run(self, stream=None):
+        _check(lib().vcsr_cusparse_run(self._h, _stream(stream)))
+
+    def close(self):
+        if self._h:
+            lib().vcsr_cusparse_destroy(self._h)
+            self._h = None
+
+    __del__ = close
+
+
+class Plan:
+    """Build-once SpMM operator (vcsr_plan_*).  csr is a host CSR or a DeviceCSR."""
+
+    def __init__(self, csr, segw=4, bundle=32, tileK=0, max_O=512, vec_rows=0,
+                 chunk=0, reference_format=False, stream=None):
+        L = lib()
+        p = _PlanParams()
+        L.vcsr_plan_params_default(C.byref(p))
+        p.segw, p.bundle, p.tileK, p.max_O = segw, bundle, tileK, max_O
+        p.vec_rows, p.chunk = vec_rows, chunk
+        p.flags = PLAN_REFERENCE_FORMAT if reference_format else 0
+        where = DEVICE if isinstance(csr, DeviceCSR) else HOST
+        s = csr._struct()
+        h = C.c_void_p()
+        _check(L.vcsr_plan_create(C.byref(s), where, C.byref(p), C.byref(h),
+                                  _stream(stream)))
+        self._h = h
+        self.M, self.N, self.nnz = csr.M, csr.N, csr.nnz
+        self.last_launches = 0
+
+    def info(self):
+        i = _PlanInfo()
+        _check(lib().vcsr_plan_get_info(self._h, C.byref(i)))
+        return {k: getattr(i, k) for k, _ in _PlanInfo._fields_}
+
+    def export(self) -> VCSRSpMM:
+        v = _Vcsr()
+        _check(lib().vcsr_plan_export(self._h, C.byref(v)))
+        return _vcsr_from_host_struct(v)
+
+    def spmm(self, B, Cout, O=None, ldb=None, ldc=None, stream=None):
+        """C = A*B on device tensors (or raw pointers with O/ldb/ldc given)."""
+        if O is None:
+            O = B.shape[1]
+        if ldb is None:
+            ldb = B.stride(0) if hasattr(B, "stride") else O
+        if ldc is None:
+            ldc = Cout.stride(0) if hasattr(Cout, "stride") else O
+        n = C.c_int(0)
+        _check(lib().vcsr_spmm(self._h, _ptr(B), ldb, _ptr(Cout), ldc, O,
+                               _stream(stream), C.byref(n)))
+        self.last_launches = n.value
+        return Cout
+
+    def spmm_host(self, hB, hC, stream=None):
+        """C = A*B with host buffers (H2D, SpMM, D2H, synchronise)."""
+        O = hB.shape[1] if hB is not None else hC.shape[1]
+        _check(lib().vcsr_spmm_host(self._h, _ptr(hB), _ptr(hC), O, _stream(stream)))
+        return hC
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().vcsr_plan_destroy(self._h)
+            self._h = None
+
+    __del__ = close
