@@ -25,7 +25,6 @@ import argparse
 import json
 import os
 import re
-import subprocess
 import sys
 import time
 
@@ -91,57 +90,52 @@ def profile_traffic(label):
 
 
 class Clocks:
-    """nvidia-smi sampling during the timed region."""
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock and clock-event reasons sampled through NVML every ~0.5 ms in
+    a background thread while the timed region runs."""
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown"}
 
-    def __init__(self, gpu_id):
-        self.index = gpu_id  # UUID (survives CUDA_VISIBLE_DEVICES remapping)
-        self.proc = None
-        self.path = f"/tmp/vcsr_clocks_{os.getpid()}.csv"
+    def __init__(self, uuid):
+        self.uuid = uuid
+        self.samples = []
+        self.reasons = 0
+        self.thread = None
+        self.stop_flag = False
+        self.max_mhz = None
 
     def start(self):
+        import threading
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            import pynvml as N
+            N.nvmlInit()
+            h = N.nvmlDeviceGetHandleByUUID(self.uuid)
+            self.max_mhz = float(N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM))
         except Exception:
-            self.proc = None
+            self.thread = None
+            return
+
+        def loop():
+            while not self.stop_flag:
+                try:
+                    self.samples.append(float(N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM)))
+                    self.reasons |= int(N.nvmlDeviceGetCurrentClocksEventReasons(h))
+                except Exception:
+                    pass
+                time.sleep(0.0005)
+
+        self.thread = threading.Thread(target=loop, daemon=True)
+        self.thread.start()
 
     def stop(self):
-        if self.proc is None:
+        if self.thread is None:
             return None
-        time.sleep(0.25)
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
-                 "sw_power_cap"]
-        try:
-            for line in open(self.path):
-                f = [x.strip() for x in line.split(",")]
-                if len(f) < 9:
-                    continue
-                try:
-                    sm.append(float(f[1]))
-                    mx = float(f[2])
-                except ValueError:
-                    continue
-                for n, v in zip(names, f[5:9]):
-                    if v.lower() == "active":
-                        reasons.add(n)
-            os.unlink(self.path)
-        except OSError:
+        self.stop_flag = True
+        self.thread.join(timeout=5)
+        if not self.samples:
             return None
-        if not sm:
-            return None
-        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        return {"sm_mhz": float(np.median(self.samples)), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(v for k, v in self.REASONS.items() if self.reasons & k),
+                "samples": len(self.samples), "source": "nvml"}
 
 
 def algorithmic_bytes(csr, O):
@@ -280,7 +274,7 @@ def run_ours(args):
         uuid = str(torch.cuda.get_device_properties(dev).uuid)
         gpu_id = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
     except Exception:
-        gpu_id = str(local)
+        gpu_id = ""
     clocks = Clocks(gpu_id)
     clocks.start()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]

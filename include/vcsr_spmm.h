@@ -171,6 +171,7 @@ typedef struct vcsr_plan_info {
   int num_units;      /* nnz-balanced work units */
   int num_split_vectors;
   int num_split_units;
+  int num_long_units;  /* units walked by a whole warp (>= 128 union columns) */
   int64_t panel_bytes; /* device bytes of the panel layout */
   int has_reference_format;
   double build_ms;    /* wall time of vcsr_plan_create */
@@ -244,6 +245,30 @@ vcsr_status vcsr_partition_rows(const int *row_ptr, int M, int parts,
 /* Extract rows [r0, r1) of a host CSR as a new host CSR (row ids local). */
 vcsr_status vcsr_csr_row_panel(const vcsr_csr *csr, int r0, int r1,
                                vcsr_csr *out);
+
+/* Row panels of A on several GPUs of one process.  No reference counterpart
+ * (the reference runs on device 0 only, src/kernels.cu:129); the survey's
+ * multi-GPU design: nnz-balanced row panels (vcsr_partition_rows, align =
+ * bundle), one plan per device, B replicated by one ncclBroadcast over
+ * NVLink, disjoint C panels (no reduction).  NCCL is loaded at run time
+ * (libnccl.so.2); every wait on a collective is bounded (60 s), after which
+ * the communicators are aborted and VCSR_ERR_TIMEOUT is returned. */
+typedef struct vcsr_mgpu vcsr_mgpu;
+vcsr_status vcsr_mgpu_create(const vcsr_csr *host_csr, int ngpus,
+                             const int *devices, const vcsr_plan_params *params,
+                             vcsr_mgpu **out);
+/* Copy host B (N x O, ld = O) to the first device and broadcast it to all;
+ * *bcast_ms = time of the broadcast (max over devices). */
+vcsr_status vcsr_mgpu_set_b(vcsr_mgpu *m, const float *hB, int O,
+                            float *bcast_ms);
+/* Every device computes its C panel; *ms = max over devices of the kernel
+ * time measured with CUDA events. */
+vcsr_status vcsr_mgpu_spmm(vcsr_mgpu *m, int O, float *ms);
+/* Copy the C panels to host C (M x O, ld = O). */
+vcsr_status vcsr_mgpu_gather_c(vcsr_mgpu *m, float *hC);
+/* Row cut points (ngpus + 1 entries) of the panels. */
+vcsr_status vcsr_mgpu_cuts(const vcsr_mgpu *m, int *cuts);
+void vcsr_mgpu_destroy(vcsr_mgpu *m);
 
 #ifdef __cplusplus
 }

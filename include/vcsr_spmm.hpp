@@ -1,0 +1,196 @@
+// vcsr_spmm.hpp — header-only C++ shim with the reference's host interface,
+// implemented over the C ABI (vcsr_spmm.h), so callers written against
+// include/mmio.hpp, include/csr.hpp, include/vcsr.hpp and the launchers in
+// src/kernels.cu compile and link unchanged (link with -lvcsr_b200 -lcudart).
+//
+// Kept alike on purpose: struct and field names, argument order and meaning,
+// and error behaviour (std::runtime_error where the reference throws).
+// Different on purpose: csr_to_vcsr_spmm runs on the GPU and orders rows of
+// equal per-segment count by row index; run_vcsr_spmm_gpu adds into C without
+// the reference kernel's data race.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "vcsr_spmm.h"
+
+namespace vcsr_detail {
+inline void check(vcsr_status s) {
+  if (s != VCSR_OK) throw std::runtime_error(vcsr_last_error());
+}
+template <class T>
+inline std::vector<T> take(T *p, size_t n) {
+  return p ? std::vector<T>(p, p + n) : std::vector<T>();
+}
+}  // namespace vcsr_detail
+
+// struct COO (include/mmio.hpp:15-19)
+struct COO {
+  int M{0}, N{0};
+  std::vector<int> rows, cols;
+  std::vector<float> vals;
+};
+
+// struct CSR (include/csr.hpp:8-13)
+struct CSR {
+  int M{0}, N{0}, nnz{0};
+  std::vector<int> row_ptr;
+  std::vector<int> col;
+  std::vector<float> val;
+};
+
+// struct VCSRSpMM (include/vcsr.hpp:12-23)
+struct VCSRSpMM {
+  int M{0}, N{0};
+  int segw{4};
+  int bundle{32};
+  std::vector<int> group_ptr;
+  std::vector<int> group_depth;
+  std::vector<int> group_seg_base;
+  std::vector<int> group_rows;
+  std::vector<int> lcol;
+  std::vector<float> val;
+};
+
+// read_matrix_market_coo (include/mmio.hpp:22-45)
+inline COO read_matrix_market_coo(const std::string &path) {
+  vcsr_coo c{};
+  vcsr_detail::check(vcsr_read_mtx(path.c_str(), &c));
+  COO o;
+  o.M = c.M; o.N = c.N;
+  o.rows = vcsr_detail::take(c.rows, (size_t)c.nnz);
+  o.cols = vcsr_detail::take(c.cols, (size_t)c.nnz);
+  o.vals = vcsr_detail::take(c.vals, (size_t)c.nnz);
+  vcsr_coo_free(&c);
+  return o;
+}
+
+// coo_to_csr (include/csr.hpp:16-37)
+inline CSR coo_to_csr(const COO &coo) {
+  vcsr_coo c{coo.M, coo.N, (int)coo.vals.size(), const_cast<int *>(coo.rows.data()),
+             const_cast<int *>(coo.cols.data()), const_cast<float *>(coo.vals.data())};
+  vcsr_csr r{};
+  vcsr_detail::check(vcsr_coo_to_csr(&c, &r));
+  CSR o;
+  o.M = r.M; o.N = r.N; o.nnz = r.nnz;
+  o.row_ptr = vcsr_detail::take(r.row_ptr, (size_t)r.M + 1);
+  o.col = vcsr_detail::take(r.col, (size_t)r.nnz);
+  o.val = vcsr_detail::take(r.val, (size_t)r.nnz);
+  vcsr_csr_free(&r, VCSR_HOST);
+  return o;
+}
+
+inline vcsr_csr as_view(const CSR &c) {
+  return vcsr_csr{c.M, c.N, c.nnz, const_cast<int *>(c.row_ptr.data()),
+                  const_cast<int *>(c.col.data()), const_cast<float *>(c.val.data())};
+}
+
+// csr_to_vcsr_spmm (include/vcsr.hpp:25-109), built on the current GPU.
+inline VCSRSpMM csr_to_vcsr_spmm(const CSR &csr, int segw = 4, int bundle = 32) {
+  if (bundle <= 0) throw std::runtime_error("bundle must be >0");
+  vcsr_csr h = as_view(csr), d{};
+  vcsr_detail::check(vcsr_csr_to_device(&h, &d, nullptr));
+  vcsr_vcsr dv{}, hv{};
+  vcsr_status s = vcsr_build_vcsr(&d, segw, bundle, &dv, nullptr);
+  vcsr_csr_free(&d, VCSR_DEVICE);
+  vcsr_detail::check(s);
+  s = vcsr_vcsr_to_host(&dv, &hv);
+  vcsr_vcsr_free(&dv, VCSR_DEVICE);
+  vcsr_detail::check(s);
+  VCSRSpMM v;
+  v.M = hv.M; v.N = hv.N; v.segw = hv.segw; v.bundle = hv.bundle;
+  const size_t G = (size_t)hv.num_groups, P = (size_t)hv.num_slots;
+  v.group_ptr = vcsr_detail::take(hv.group_ptr, G + 1);
+  v.group_depth = vcsr_detail::take(hv.group_depth, G);
+  v.group_seg_base = vcsr_detail::take(hv.group_seg_base, G);
+  v.group_rows = vcsr_detail::take(hv.group_rows, G * (size_t)hv.bundle);
+  v.lcol = vcsr_detail::take(hv.lcol, P);
+  v.val = vcsr_detail::take(hv.val, P);
+  vcsr_vcsr_free(&hv, VCSR_HOST);
+  return v;
+}
+
+// run_csr_spmm_gpu (src/kernels.cu:107-118): C = A*B, times the launch.
+inline void run_csr_spmm_gpu(const int M, const int *d_rowptr, const int *d_col,
+                             const float *d_val, const float *dB, int O, float *dC,
+                             cudaStream_t st, float &ms) {
+  cudaEvent_t a, b;
+  cudaEventCreate(&a);
+  cudaEventCreate(&b);
+  cudaEventRecord(a, st);
+  vcsr_status s = vcsr_csr_spmm(M, d_rowptr, d_col, d_val, dB, O, dC, st);
+  cudaEventRecord(b, st);
+  cudaEventSynchronize(b);
+  cudaEventElapsedTime(&ms, a, b);
+  cudaEventDestroy(a);
+  cudaEventDestroy(b);
+  vcsr_detail::check(s);
+}
+
+// run_vcsr_spmm_gpu (src/kernels.cu:120-167): uploads V, C += A*B, times the
+// kernel only, frees the upload.
+inline void run_vcsr_spmm_gpu(const VCSRSpMM &V, const float *dB, int O, int tileK,
+                              float *dC, cudaStream_t st, float &ms) {
+  vcsr_vcsr d{};
+  d.M = V.M; d.N = V.N; d.segw = V.segw; d.bundle = V.bundle;
+  d.num_groups = (int)V.group_depth.size();
+  d.num_slots = (int64_t)V.lcol.size();
+  d.num_segments = (V.N + V.segw - 1) / V.segw;
+  auto up = [&](auto **dst, const auto &src) {
+    using T = typename std::remove_reference<decltype(src)>::type::value_type;
+    cudaMallocAsync((void **)dst, sizeof(T) * (src.size() ? src.size() : 1), st);
+    if (!src.empty())
+      cudaMemcpyAsync(*dst, src.data(), sizeof(T) * src.size(), cudaMemcpyHostToDevice, st);
+  };
+  up(&d.group_ptr, V.group_ptr);
+  up(&d.group_depth, V.group_depth);
+  up(&d.group_seg_base, V.group_seg_base);
+  up(&d.group_rows, V.group_rows);
+  up(&d.lcol, V.lcol);
+  up(&d.val, V.val);
+  cudaEvent_t a, b;
+  cudaEventCreate(&a);
+  cudaEventCreate(&b);
+  cudaEventRecord(a, st);
+  vcsr_status s = vcsr_spmm_segmented(&d, dB, O, tileK, dC, st);
+  cudaEventRecord(b, st);
+  cudaEventSynchronize(b);
+  cudaEventElapsedTime(&ms, a, b);
+  cudaEventDestroy(a);
+  cudaEventDestroy(b);
+  cudaFreeAsync(d.group_ptr, st); cudaFreeAsync(d.group_depth, st);
+  cudaFreeAsync(d.group_seg_base, st); cudaFreeAsync(d.group_rows, st);
+  cudaFreeAsync(d.lcol, st); cudaFreeAsync(d.val, st);
+  vcsr_detail::check(s);
+}
+
+// run_cusparse_spmm (src/kernels.cu:170-235): returns the SpMM time in ms.
+inline float run_cusparse_spmm(const int M, const int N, const int nnz,
+                               const int *d_rowptr, const int *d_col,
+                               const float *d_val, const float *dB, int O, float *dC) {
+  cudaStream_t st;
+  cudaStreamCreate(&st);
+  vcsr_cusparse *h = nullptr;
+  vcsr_status s = vcsr_cusparse_create(M, N, nnz, d_rowptr, d_col, d_val, dB, O, dC, 0,
+                                       st, &h);
+  float ms = 0.f;
+  if (s == VCSR_OK) {
+    cudaEvent_t a, b;
+    cudaEventCreate(&a);
+    cudaEventCreate(&b);
+    cudaEventRecord(a, st);
+    s = vcsr_cusparse_run(h, st);
+    cudaEventRecord(b, st);
+    cudaEventSynchronize(b);
+    cudaEventElapsedTime(&ms, a, b);
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    vcsr_cusparse_destroy(h);
+  }
+  cudaStreamDestroy(st);
+  vcsr_detail::check(s);
+  return ms;
+}

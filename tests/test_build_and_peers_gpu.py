@@ -169,3 +169,48 @@ def test_oracle_pinned_to_reference_csr_kernel():
         ref = oracle.csr_spmm_f32(csr.M, csr.row_ptr, csr.col, csr.val, B)
         got = dC.cpu().numpy() + 0.0
         assert np.array_equal(got.view(np.int32), (ref + 0.0).view(np.int32)), cfg
+
+
+def test_multi_gpu_row_panels():
+    """vcsr_mgpu_*: nnz-balanced row panels, B by NCCL broadcast, C panels
+    gathered; runs on every visible GPU (one on a single-GPU box)."""
+    n = min(torch.cuda.device_count(), 8)
+    csr = V.gen_csr("powerlaw", 0, 60000)
+    B = V.gen_dense_host(csr.N, 64, 13)
+    mg = V.MultiGPU(csr, n, bundle=32)
+    cuts = mg.cuts()
+    assert cuts[0] == 0 and cuts[-1] == csr.M and len(cuts) == n + 1
+    bms = mg.set_b(B)
+    assert bms >= 0
+    ms = mg.spmm()
+    assert ms > 0
+    C = mg.gather_c()
+    ref = oracle.csr_spmm_f64(csr.M, csr.row_ptr, csr.col, csr.val, B)
+    assert rel_l2(C, ref) <= 1e-5
+    mg.close()
+
+
+def test_cli_drop_in(tmp_path):
+    """spmm_vcsr with the reference's flags prints the table and the
+    'Name: <ms> ms <gflops> GFLOP/s [..]' lines the reference scripts parse."""
+    import os
+    import subprocess
+    from helpers import ROOT
+    exe = os.path.join(ROOT, "vcsr-spmm_b200", "bin", "spmm_vcsr")
+    mtx = os.path.join(ROOT, "tests", "golden", "mtx", "empty_rows.mtx")
+    out = subprocess.run([exe, "--mtx", mtx, "--O", "8", "--segw", "4", "--bundle", "32",
+                          "--tileK", "64", "--repeat", "3", "--algo", "all", "--check"],
+                         capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0, out.stderr
+    lines = out.stdout.strip().splitlines()
+    assert any(l.startswith("Matrix: 8 x 10, nnz=7") for l in lines)
+    tail = lines[-1].split()
+    assert "ms" in tail and "GFLOP/s" in tail
+    rel = [float(l.split("=")[-1]) for l in lines if "rel_l2" in l]
+    assert rel and max(rel) < 1e-5
+    g = subprocess.run([exe, "--gen", "fem", "--size", "3000", "--O", "32", "--algo", "vcsr",
+                        "--repeat", "2"], capture_output=True, text=True, timeout=120)
+    assert g.returncode == 0 and "VCSR:" in g.stdout.splitlines()[-1]
+    bad = subprocess.run([exe, "--mtx", "/nonexistent.mtx", "--O", "8"], capture_output=True,
+                         text=True, timeout=60)
+    assert bad.returncode != 0 and "Failed to open MTX" in bad.stderr

@@ -139,7 +139,7 @@ vcsr_status build_panel_host(const vcsr_csr &csr, int R, int chunk, int sms,
   if (chunk <= 0) {
     const int64_t total = out->vec_ptr[V];
     const int64_t per = total / ((int64_t)(sms > 0 ? sms : 148) * 32);
-    chunk = (int)std::max<int64_t>(256, std::min<int64_t>(per, 1 << 20));
+    chunk = (int)std::max<int64_t>(256, std::min<int64_t>(per, 2048));
   }
   out->chunk = chunk;
   out->units.clear();

@@ -31,6 +31,8 @@ struct vcsr_plan {
   int *d_ucol = nullptr;
   float *d_uval = nullptr;
   int4 *d_units = nullptr;
+  int *d_short = nullptr, *d_long = nullptr;
+  int n_short = 0, n_long = 0;
   int2 *d_parts = nullptr;
   int2 *d_svecs = nullptr;
   float *d_partials = nullptr;
@@ -62,6 +64,7 @@ vcsr_status upload(T **dst, const std::vector<T> &src, cudaStream_t st,
 
 void release(vcsr_plan *p) {
   cudaFree(p->d_ucol); cudaFree(p->d_uval); cudaFree(p->d_units);
+  cudaFree(p->d_short); cudaFree(p->d_long);
   cudaFree(p->d_parts); cudaFree(p->d_svecs); cudaFree(p->d_partials);
   cudaFree(p->d_counters); cudaFree(p->d_stage_B); cudaFree(p->d_stage_C);
   if (p->has_ref) vcsr_vcsr_free(&p->ref, VCSR_DEVICE);
@@ -73,6 +76,10 @@ vcsr::PanelDevView view(const vcsr_plan *p) {
   v.uval = p->d_uval;
   v.units = p->d_units;
   v.n_units = p->n_units;
+  v.short_idx = p->d_short;
+  v.n_short = p->n_short;
+  v.long_idx = p->d_long;
+  v.n_long = p->n_long;
   v.parts = p->d_parts;
   v.svecs = p->d_svecs;
   v.partials = p->d_partials;
@@ -237,6 +244,15 @@ vcsr_status vcsr_plan_create(const vcsr_csr *csr, int csr_where,
   static_assert(sizeof(vcsr::SplitVec) == sizeof(int2), "SplitVec must match int2");
   std::vector<int4> units(ph.units.size());
   std::memcpy(units.data(), ph.units.data(), sizeof(int4) * units.size());
+  // units of at least kLongUnit union columns are walked by a whole warp
+  // (its sub-warps split the columns); the rest by one sub-warp each
+  constexpr int kLongUnit = 128;
+  std::vector<int> short_idx, long_idx;
+  for (size_t u = 0; u < ph.units.size(); ++u)
+    (ph.units[u].end - ph.units[u].begin >= kLongUnit ? long_idx : short_idx)
+        .push_back((int)u);
+  p->n_short = (int)short_idx.size();
+  p->n_long = (int)long_idx.size();
   std::vector<int2> parts(ph.parts.size()), svecs(ph.svecs.size());
   std::memcpy(parts.data(), ph.parts.data(), sizeof(int2) * parts.size());
   std::memcpy(svecs.data(), ph.svecs.data(), sizeof(int2) * svecs.size());
@@ -244,7 +260,9 @@ vcsr_status vcsr_plan_create(const vcsr_csr *csr, int csr_where,
       (s = upload(&p->d_uval, ph.uval, st, &p->panel_bytes)) ||
       (s = upload(&p->d_units, units, st, &p->panel_bytes)) ||
       (s = upload(&p->d_parts, parts, st, &p->panel_bytes)) ||
-      (s = upload(&p->d_svecs, svecs, st, &p->panel_bytes))) {
+      (s = upload(&p->d_svecs, svecs, st, &p->panel_bytes)) ||
+      (s = upload(&p->d_short, short_idx, st, &p->panel_bytes)) ||
+      (s = upload(&p->d_long, long_idx, st, &p->panel_bytes))) {
     if (owned) vcsr_csr_free(&h, VCSR_HOST);
     release(p);
     delete p;
@@ -303,6 +321,7 @@ vcsr_status vcsr_plan_get_info(const vcsr_plan *p, vcsr_plan_info *info) {
   info->num_units = p->n_units;
   info->num_split_vectors = p->n_split_vectors;
   info->num_split_units = p->n_split_units;
+  info->num_long_units = p->n_long;
   info->panel_bytes = p->panel_bytes;
   info->has_reference_format = p->has_ref ? 1 : 0;
   info->build_ms = p->build_ms;

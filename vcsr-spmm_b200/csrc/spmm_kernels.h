@@ -14,6 +14,10 @@ struct PanelDevView {
   const int4 *units = nullptr;    // {vector, begin, end, split slot or -1}
   const int *row_ptr = nullptr;   // CSR mode only
   int n_units = 0;
+  const int *short_idx = nullptr; // units walked by one sub-warp each
+  int n_short = 0;
+  const int *long_idx = nullptr;  // units walked by a whole warp
+  int n_long = 0;
   const int2 *parts = nullptr;    // per split slot: {split vector, part}
   const int2 *svecs = nullptr;    // per split vector: {first slot, nparts}
   float *partials = nullptr;      // split slots x R x pstride floats

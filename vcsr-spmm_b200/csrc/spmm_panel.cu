@@ -1,22 +1,30 @@
 // spmm_panel.cu — the row-stationary VCSR SpMM kernel for sm_100a.
 //
-// C[M x O] = A * B with A in vector panels (panel.h).  One sub-warp of L lanes
-// owns one work item = (unit, O-tile).  Lanes lie across O: lane l holds
-// columns k = tile*W + v*L*VW + l*VW (VW = 4 floats per 128-bit access, NV
-// such vectors per lane), so a B row segment is one coalesced 128-bit load per
-// lane.  The R rows of the vector accumulate in registers (C stationary) while
-// the sub-warp walks the unit's union columns in order: per column one load
-// of the column index, one 16..64-byte load of the R values (the same address
-// for the whole sub-warp) and NV B loads feed R*NV*VW FMAs per lane.  Each
-// row's FMA chain follows its CSR order, so an unsplit vector's row equals the
-// CSR reference bit for bit.  Unsplit units store C once with streaming
-// stores (beta = 0, no zero-fill pass); parts of a split vector store partial
-// sums and the last part to arrive (atomic ticket, no waiting) adds the parts
-// in part order and writes C.
+// C[M x O] = A * B with A in vector panels (panel.h).  Lanes lie across O: a
+// sub-warp of L lanes covers an O-tile of W = L*VW*NV columns (VW = 4 floats
+// per 128-bit access, NV accesses per lane), so one B row segment is one
+// coalesced 128-bit load per lane.  The R rows of a vector accumulate in
+// registers (C stationary) while the team walks the unit's union columns.
 //
-// The long-row scheme of src/aspt.cu:38-142 (a warp shares one row's entries
-// and broadcasts them) appears here as the sub-warp walking one vector, with
-// the entries read by address-uniform loads instead of __shfl_sync.
+// Per team and per chunk of union columns, the column indices and R-value
+// vectors are copied global -> shared with cp.async into one of two buffers
+// (the next chunk is in flight while the current one is consumed), so B row
+// addresses never wait on a global load; B rows are then loaded U at a time
+// per lane before the FMAs that use them.
+//
+// Two team shapes share one launch (a warp takes one work item):
+//  * a group of 32/L short units, one per sub-warp; each row's FMA chain
+//    follows its CSR order, so such rows equal the CSR reference bit for bit;
+//  * one long unit, all 32/L sub-warps of the warp ("column groups") taking
+//    every (32/L)-th union column; the column groups are then summed with a
+//    fixed xor-shuffle tree (the long-row scheme of src/aspt.cu:38-142 --
+//    a warp shares one row -- with the warp split over columns instead of
+//    the row's entries being broadcast).
+// A vector longer than the plan's chunk is split over several units; each
+// part stores its R x O partial sums and the last part to finish (atomic
+// ticket, no waiting) adds the parts in fixed order and writes C.  Results
+// are therefore deterministic run to run.  C is written, never read
+// (beta = 0), with streaming stores.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -53,6 +61,10 @@ struct VecT<4> {
   static __device__ __forceinline__ T add(T a, T b) {
     return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
   }
+  static __device__ __forceinline__ T shfl_xor(unsigned m, T v, int o) {
+    return make_float4(__shfl_xor_sync(m, v.x, o), __shfl_xor_sync(m, v.y, o),
+                       __shfl_xor_sync(m, v.z, o), __shfl_xor_sync(m, v.w, o));
+  }
 };
 template <>
 struct VecT<1> {
@@ -64,22 +76,64 @@ struct VecT<1> {
   static __device__ __forceinline__ void stcs(float *p, T v) { __stcs(p, v); }
   static __device__ __forceinline__ T fma(float a, T b, T c) { return fmaf(a, b, c); }
   static __device__ __forceinline__ T add(T a, T b) { return a + b; }
+  static __device__ __forceinline__ T shfl_xor(unsigned m, T v, int o) {
+    return __shfl_xor_sync(m, v, o);
+  }
 };
 
+// ---------------------------------------------------------------- cp.async
+__device__ __forceinline__ void cp_async4(void *smem, const void *gmem) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(s), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async8(void *smem, const void *gmem) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(s), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;\n" ::);
+}
+__device__ __forceinline__ void cp_async_wait_1() {
+  asm volatile("cp.async.wait_group 1;\n" ::);
+}
+
+// Copy union columns [c0, c0+n) of a unit into a team buffer:
+// scol[0..n) and sval[0..n*R).  Lanes t = 0..T-1 of the team share the work.
 template <int R>
-__device__ __forceinline__ void load_vals(const float *__restrict__ uval, int j,
-                                          float (&a)[R]) {
-  if constexpr (R == 1) {
-    a[0] = __ldg(uval + j);
+__device__ __forceinline__ void stage_chunk(const int *__restrict__ ucol,
+                                            const float *__restrict__ uval, int c0,
+                                            int n, int *scol, float *sval, int t,
+                                            int T) {
+  for (int i = t; i < n; i += T) cp_async4(scol + i, ucol + c0 + i);
+  if constexpr (R >= 4) {
+    const int nv = n * (R / 4);
+    const float *src = uval + (size_t)c0 * R;
+    for (int i = t; i < nv; i += T) cp_async16(sval + 4 * i, src + 4 * i);
   } else if constexpr (R == 2) {
-    const float2 t = __ldg(reinterpret_cast<const float2 *>(uval) + j);
+    const float *src = uval + (size_t)c0 * 2;
+    for (int i = t; i < n; i += T) cp_async8(sval + 2 * i, src + 2 * i);
+  } else {
+    for (int i = t; i < n; i += T) cp_async4(sval + i, uval + c0 + i);
+  }
+}
+
+template <int R>
+__device__ __forceinline__ void load_vals_smem(const float *sval, int j, float (&a)[R]) {
+  if constexpr (R == 1) {
+    a[0] = sval[j];
+  } else if constexpr (R == 2) {
+    const float2 t = reinterpret_cast<const float2 *>(sval)[j];
     a[0] = t.x;
     a[1] = t.y;
   } else {
-    const float4 *p = reinterpret_cast<const float4 *>(uval + (size_t)j * R);
+    const float4 *p = reinterpret_cast<const float4 *>(sval + j * R);
 #pragma unroll
     for (int q = 0; q < R / 4; ++q) {
-      const float4 t = __ldg(p + q);
+      const float4 t = p[q];
       a[4 * q + 0] = t.x;
       a[4 * q + 1] = t.y;
       a[4 * q + 2] = t.z;
@@ -88,86 +142,231 @@ __device__ __forceinline__ void load_vals(const float *__restrict__ uval, int j,
   }
 }
 
-template <int R, int NV, int VW, int UNROLL, bool ROWPTR>
-__global__ void __launch_bounds__(256)
-    panel_spmm_kernel(const PanelDevView P, const float *__restrict__ B, int ldb,
-                      float *__restrict__ C, int ldc, int O, int lshift,
-                      int n_otiles, int W) {
-  using V = VecT<VW>;
-  using T = typename V::T;
-  const int L = 1 << lshift;
-  const int lane = threadIdx.x & 31;
-  const int sub = lane >> lshift;
-  const int sl = lane & (L - 1);
-  const unsigned submask =
-      (L == 32) ? 0xffffffffu : (((1u << L) - 1u) << (sub * L));
-  const int subs = 32 >> lshift;
-  const long long gsw =
-      ((long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * subs + sub;
-  const long long nsw = (long long)gridDim.x * (blockDim.x >> 5) * subs;
-  const long long n_items = (long long)P.n_units * n_otiles;
+// Columns per prefetch group: B loads of group g+1 are in flight while
+// group g is consumed, so a lane holds 2 * UN * NV 128-bit B values.
+// Build-time tuning knobs (defaults measured on B200, see the design notes).
+#ifndef VCSR_UN_SMALL_R
+#define VCSR_UN_SMALL_R 8  // R <= 4, NV = 1
+#endif
+#ifndef VCSR_UN_R8
+#define VCSR_UN_R8 4       // R = 8, NV = 1
+#endif
+#ifndef VCSR_PANEL_MIN_BLOCKS
+#define VCSR_PANEL_MIN_BLOCKS 1
+#endif
+template <int R, int NV>
+constexpr int unroll_for() {
+  return R <= 4 ? (NV == 1 ? VCSR_UN_SMALL_R : VCSR_UN_SMALL_R / 2)
+                : (R == 8 ? (NV == 1 ? VCSR_UN_R8 : VCSR_UN_R8 / 2) : 2);
+}
 
-  for (long long item = gsw; item < n_items; item += nsw) {
-    const int u = (int)(item / n_otiles);
-    const int ot = (int)(item - (long long)u * n_otiles);
-    int4 U;
-    if constexpr (ROWPTR) {
-      U = make_int4(u, __ldg(P.row_ptr + u), __ldg(P.row_ptr + u + 1), -1);
+// Accumulators.  With 128-bit lanes the sums are kept as float2 pairs so that
+// one packed FFMA2 (__ffma2_rn: two round-to-nearest fused multiply-adds,
+// bit-identical to two fmaf) does two updates: pairs of rows (r, r+1) at one
+// column when R >= 2, pairs of columns of one row when R = 1.  The scalar
+// path (VW = 1) keeps one float per row.
+template <int R, int NV, int VW>
+struct Acc;
+
+template <int R, int NV>
+struct Acc<R, NV, 4> {
+  static constexpr bool kRowPairs = R >= 2;
+  static constexpr int kP = kRowPairs ? R / 2 : 1;
+  static constexpr int kC = kRowPairs ? 4 : 2;
+  float2 p[kP][NV][kC];
+  __device__ __forceinline__ void zero() {
+#pragma unroll
+    for (int i = 0; i < kP; ++i)
+#pragma unroll
+      for (int v = 0; v < NV; ++v)
+#pragma unroll
+        for (int c = 0; c < kC; ++c) p[i][v][c] = make_float2(0.f, 0.f);
+  }
+  // one union column: values a[R] of the R rows, B values b[NV]
+  __device__ __forceinline__ void fma(const float (&a)[R], const float4 (&b)[NV]) {
+    if constexpr (kRowPairs) {
+#pragma unroll
+      for (int v = 0; v < NV; ++v) {
+        const float2 bx = make_float2(b[v].x, b[v].x), by = make_float2(b[v].y, b[v].y);
+        const float2 bz = make_float2(b[v].z, b[v].z), bw = make_float2(b[v].w, b[v].w);
+#pragma unroll
+        for (int i = 0; i < kP; ++i) {
+          const float2 ar = make_float2(a[2 * i], a[2 * i + 1]);
+          p[i][v][0] = __ffma2_rn(ar, bx, p[i][v][0]);
+          p[i][v][1] = __ffma2_rn(ar, by, p[i][v][1]);
+          p[i][v][2] = __ffma2_rn(ar, bz, p[i][v][2]);
+          p[i][v][3] = __ffma2_rn(ar, bw, p[i][v][3]);
+        }
+      }
     } else {
-      U = __ldg(P.units + u);
+      const float2 aa = make_float2(a[0], a[0]);
+#pragma unroll
+      for (int v = 0; v < NV; ++v) {
+        p[0][v][0] = __ffma2_rn(aa, make_float2(b[v].x, b[v].y), p[0][v][0]);
+        p[0][v][1] = __ffma2_rn(aa, make_float2(b[v].z, b[v].w), p[0][v][1]);
+      }
     }
-    int kk[NV];
-    bool ok[NV];
+  }
+  __device__ __forceinline__ void store(float4 (&out)[R][NV]) const {
 #pragma unroll
     for (int v = 0; v < NV; ++v) {
-      kk[v] = ot * W + v * (L * VW) + sl * VW;
-      ok[v] = kk[v] < O;
+      if constexpr (kRowPairs) {
+#pragma unroll
+        for (int i = 0; i < kP; ++i) {
+          out[2 * i][v] = make_float4(p[i][v][0].x, p[i][v][1].x, p[i][v][2].x, p[i][v][3].x);
+          out[2 * i + 1][v] = make_float4(p[i][v][0].y, p[i][v][1].y, p[i][v][2].y, p[i][v][3].y);
+        }
+      } else {
+        out[0][v] = make_float4(p[0][v][0].x, p[0][v][0].y, p[0][v][1].x, p[0][v][1].y);
+      }
     }
-    T acc[R][NV];
+  }
+};
+
+template <int R, int NV>
+struct Acc<R, NV, 1> {
+  float s[R][NV];
+  __device__ __forceinline__ void zero() {
 #pragma unroll
     for (int r = 0; r < R; ++r)
 #pragma unroll
-      for (int v = 0; v < NV; ++v) acc[r][v] = V::zero();
+      for (int v = 0; v < NV; ++v) s[r][v] = 0.f;
+  }
+  __device__ __forceinline__ void fma(const float (&a)[R], const float (&b)[NV]) {
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int v = 0; v < NV; ++v) s[r][v] = fmaf(a[r], b[v], s[r][v]);
+  }
+  __device__ __forceinline__ void store(float (&out)[R][NV]) const {
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int v = 0; v < NV; ++v) out[r][v] = s[r][v];
+  }
+};
 
-    int j = U.y;
-    const int end = U.z;
-    for (; j + UNROLL <= end; j += UNROLL) {
-      int c[UNROLL];
-      float a[UNROLL][R];
-      T b[UNROLL][NV];
+// B values of UN columns j0, j0+step, ...; FULL = all UN exist.
+template <int NV, int VW, int UN, bool FULL>
+__device__ __forceinline__ void load_group(const float *__restrict__ Bk, int ldb,
+                                           const int *scol, int j0, int step, int n,
+                                           const bool (&ok)[NV], int vstride,
+                                           typename VecT<VW>::T (&b)[UN][NV]) {
+  using V = VecT<VW>;
 #pragma unroll
-      for (int q = 0; q < UNROLL; ++q) c[q] = __ldg(P.ucol + j + q);
+  for (int q = 0; q < UN; ++q) {
+    const int j = j0 + q * step;
+    if (FULL || j < n) {
+      const float *bp = Bk + (size_t)scol[j] * ldb;
 #pragma unroll
-      for (int q = 0; q < UNROLL; ++q) load_vals<R>(P.uval, j + q, a[q]);
-#pragma unroll
-      for (int q = 0; q < UNROLL; ++q) {
-        const float *bp = B + (size_t)c[q] * ldb;
-#pragma unroll
-        for (int v = 0; v < NV; ++v) b[q][v] = ok[v] ? V::ld(bp + kk[v]) : V::zero();
-      }
-#pragma unroll
-      for (int q = 0; q < UNROLL; ++q)
-#pragma unroll
-        for (int r = 0; r < R; ++r)
-#pragma unroll
-          for (int v = 0; v < NV; ++v) acc[r][v] = V::fma(a[q][r], b[q][v], acc[r][v]);
+      for (int v = 0; v < NV; ++v) b[q][v] = ok[v] ? V::ld(bp + v * vstride) : V::zero();
     }
-    for (; j < end; ++j) {
-      const int c = __ldg(P.ucol + j);
+  }
+}
+
+template <int R, int NV, int VW, int UN, bool FULL>
+__device__ __forceinline__ void fma_group(const float *sval, int j0, int step, int n,
+                                          const typename VecT<VW>::T (&b)[UN][NV],
+                                          Acc<R, NV, VW> &acc) {
+#pragma unroll
+  for (int q = 0; q < UN; ++q) {
+    const int j = j0 + q * step;
+    if (FULL || j < n) {
       float a[R];
-      load_vals<R>(P.uval, j, a);
-      const float *bp = B + (size_t)c * ldb;
-      T b[NV];
-#pragma unroll
-      for (int v = 0; v < NV; ++v) b[v] = ok[v] ? V::ld(bp + kk[v]) : V::zero();
-#pragma unroll
-      for (int r = 0; r < R; ++r)
-#pragma unroll
-        for (int v = 0; v < NV; ++v) acc[r][v] = V::fma(a[r], b[v], acc[r][v]);
+      load_vals_smem<R>(sval, j, a);
+      acc.fma(a, b[q]);
     }
+  }
+}
 
-    const int row0 = U.x * R;
-    if (U.w < 0) {
+// One team walks one unit.  cg / ncg: this lane's column group and the number
+// of column groups (1 for a sub-warp team); t / T: lane index and size of the
+// team for staging; tmask: the team's lanes.  Leaves the column-group sums
+// reduced into the lanes of every column group.
+template <int R, int NV, int VW>
+__device__ __forceinline__ void walk_unit(
+    const PanelDevView &P, const float *__restrict__ B, int ldb, const int4 &U,
+    const int (&kk)[NV], const bool (&ok)[NV], int cg, int ncg, int t, int T,
+    unsigned tmask, int L, int chunk, int *buf_col, float *buf_val,
+    typename VecT<VW>::T (&out)[R][NV]) {
+  using V = VecT<VW>;
+  using Tv = typename V::T;
+  constexpr int UN = unroll_for<R, NV>();
+  Acc<R, NV, VW> acc;
+  acc.zero();
+  const float *Bk = B + kk[0];
+  const int vstride = L * VW;
+  const int begin = U.y, end = U.z;
+  if (begin < end) {
+    // prologue: stage chunk 0 into buffer 0
+    int n0 = min(chunk, end - begin);
+    stage_chunk<R>(P.ucol, P.uval, begin, n0, buf_col, buf_val, t, T);
+    cp_async_commit();
+    int cur = 0;
+    for (int c0 = begin; c0 < end; c0 += chunk) {
+      const int n = min(chunk, end - c0);
+      const int nx = c0 + chunk < end ? min(chunk, end - c0 - chunk) : 0;
+      int *ncol = buf_col + (cur ^ 1) * chunk;
+      float *nval = buf_val + (size_t)(cur ^ 1) * chunk * R;
+      if (nx > 0) stage_chunk<R>(P.ucol, P.uval, c0 + chunk, nx, ncol, nval, t, T);
+      cp_async_commit();
+      cp_async_wait_1();
+      __syncwarp(tmask);
+      const int *scol = buf_col + cur * chunk;
+      const float *sval = buf_val + (size_t)cur * chunk * R;
+      // this column group's columns: cg, cg+ncg, ...; full groups of UN of
+      // them are pipelined two deep, the remainder is one guarded group
+      const int mine = cg < n ? (n - cg + ncg - 1) / ncg : 0;
+      const int nfull = mine / UN;
+      const int gstep = UN * ncg;
+      Tv b0[UN][NV], b1[UN][NV];
+      int j = cg;
+      if (nfull > 0)
+        load_group<NV, VW, UN, true>(Bk, ldb, scol, j, ncg, n, ok, vstride, b0);
+      for (int g = 0; g < nfull; g += 2) {
+        if (g + 1 < nfull)
+          load_group<NV, VW, UN, true>(Bk, ldb, scol, j + gstep, ncg, n, ok, vstride, b1);
+        fma_group<R, NV, VW, UN, true>(sval, j, ncg, n, b0, acc);
+        if (g + 1 >= nfull) {
+          j += gstep;
+          break;
+        }
+        if (g + 2 < nfull)
+          load_group<NV, VW, UN, true>(Bk, ldb, scol, j + 2 * gstep, ncg, n, ok, vstride,
+                                       b0);
+        fma_group<R, NV, VW, UN, true>(sval, j + gstep, ncg, n, b1, acc);
+        j += 2 * gstep;
+      }
+      if (j < n) {
+        load_group<NV, VW, UN, false>(Bk, ldb, scol, j, ncg, n, ok, vstride, b0);
+        fma_group<R, NV, VW, UN, false>(sval, j, ncg, n, b0, acc);
+      }
+      __syncwarp(tmask);  // everyone is done with `cur` before it is refilled
+      cur ^= 1;
+    }
+  }
+  acc.store(out);
+  // sum the column groups: fixed xor tree over the lane bits above L
+  for (int off = L; off < L * ncg; off <<= 1) {
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int v = 0; v < NV; ++v) out[r][v] = V::add(out[r][v], V::shfl_xor(tmask, out[r][v], off));
+  }
+}
+
+// Store a finished unit: straight to C, or (split vector) publish the part
+// and let the last part reduce all parts into C.
+template <int R, int NV, int VW>
+__device__ __forceinline__ void finish_unit(
+    const PanelDevView &P, float *__restrict__ C, int ldc, const int4 &U, int ot,
+    const int (&kk)[NV], const bool (&ok)[NV], int cg, int ncg, int lead_lane,
+    unsigned tmask, typename VecT<VW>::T (&acc)[R][NV]) {
+  using V = VecT<VW>;
+  using Tv = typename V::T;
+  const int row0 = U.x * R;
+  if (U.w < 0) {
+    if (cg == 0) {
 #pragma unroll
       for (int r = 0; r < R; ++r) {
         const int row = row0 + r;
@@ -177,51 +376,148 @@ __global__ void __launch_bounds__(256)
             if (ok[v]) V::stcs(C + (size_t)row * ldc + kk[v], acc[r][v]);
         }
       }
-    } else {
-      // split vector: publish this part, last part to arrive reduces
-      const int slot = U.w;
-      float *part = P.partials + (size_t)slot * R * P.pstride;
+    }
+    return;
+  }
+  const int slot = U.w;
+  if (cg == 0) {
+    float *part = P.partials + (size_t)slot * R * P.pstride;
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int v = 0; v < NV; ++v)
+        if (ok[v]) V::st(part + (size_t)r * P.pstride + kk[v], acc[r][v]);
+  }
+  __threadfence();
+  __syncwarp(tmask);
+  const int2 sp = __ldg(P.parts + slot);   // {split vector, part}
+  const int2 svi = __ldg(P.svecs + sp.x);  // {first slot, nparts}
+  int *ctr = P.counters + (size_t)sp.x * P.counter_stride + ot;
+  int ticket = 0;
+  if ((threadIdx.x & 31) == lead_lane) ticket = atomicAdd(ctr, 1);
+  ticket = __shfl_sync(tmask, ticket, lead_lane);
+  if (ticket != svi.y - 1) return;
+  __threadfence();
+  // last part: column group g sums parts g, g+ncg, ... with four independent
+  // chains, then the groups are summed by the fixed xor tree
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      Tv s0 = V::zero(), s1 = V::zero(), s2 = V::zero(), s3 = V::zero();
+      if (ok[v]) {
+        const float *base = P.partials + (size_t)svi.x * R * P.pstride +
+                            (size_t)r * P.pstride + kk[v];
+        const size_t step = (size_t)R * P.pstride;
+        int p = cg;
+        for (; p + 3 * ncg < svi.y; p += 4 * ncg) {
+          s0 = V::add(s0, V::ldcg(base + (size_t)p * step));
+          s1 = V::add(s1, V::ldcg(base + (size_t)(p + ncg) * step));
+          s2 = V::add(s2, V::ldcg(base + (size_t)(p + 2 * ncg) * step));
+          s3 = V::add(s3, V::ldcg(base + (size_t)(p + 3 * ncg) * step));
+        }
+        for (; p < svi.y; p += ncg) s0 = V::add(s0, V::ldcg(base + (size_t)p * step));
+      }
+      acc[r][v] = V::add(V::add(s0, s1), V::add(s2, s3));
+    }
+  }
+  const int L32 = 32 / ncg;  // lanes per column group
+  if (ncg > 1) {
+    for (int off = L32; off < 32; off <<= 1) {
 #pragma unroll
       for (int r = 0; r < R; ++r)
 #pragma unroll
+        for (int v = 0; v < NV; ++v) acc[r][v] = V::add(acc[r][v], V::shfl_xor(tmask, acc[r][v], off));
+    }
+  }
+  if (cg == 0) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int row = row0 + r;
+      if (row < P.M) {
+#pragma unroll
         for (int v = 0; v < NV; ++v)
-          if (ok[v]) V::st(part + (size_t)r * P.pstride + kk[v], acc[r][v]);
-      __threadfence();
-      __syncwarp(submask);
-      const int2 sp = __ldg(P.parts + slot);       // {split vector, part}
-      const int2 svi = __ldg(P.svecs + sp.x);      // {first slot, nparts}
-      int ticket = 0;
-      int *ctr = P.counters + (size_t)sp.x * P.counter_stride + ot;
-      if (sl == 0) ticket = atomicAdd(ctr, 1);
-      ticket = __shfl_sync(submask, ticket, 0, L);
-      if (ticket == svi.y - 1) {
-        __threadfence();
-#pragma unroll
-        for (int r = 0; r < R; ++r) {
-          const int row = row0 + r;
-          if (row >= P.M) continue;
-#pragma unroll
-          for (int v = 0; v < NV; ++v) {
-            if (!ok[v]) continue;
-            T s = V::zero();
-            for (int p = 0; p < svi.y; ++p)
-              s = V::add(s, V::ldcg(P.partials +
-                                    ((size_t)(svi.x + p) * R + r) * P.pstride + kk[v]));
-            V::stcs(C + (size_t)row * ldc + kk[v], s);
-          }
-        }
-        if (sl == 0) *ctr = 0;  // ready for the next launch
+          if (ok[v]) V::stcs(C + (size_t)row * ldc + kk[v], acc[r][v]);
       }
     }
   }
+  if ((threadIdx.x & 31) == lead_lane) *ctr = 0;  // ready for the next launch
 }
 
-using KernelFn = void (*)(const PanelDevView, const float *, int, float *, int,
+template <int R, int NV, int VW, bool ROWPTR>
+__global__ void __launch_bounds__(256, VCSR_PANEL_MIN_BLOCKS)
+    panel_spmm_kernel(const PanelDevView P, const float *__restrict__ B, int ldb,
+                      float *__restrict__ C, int ldc, int O, int lshift,
+                      int n_otiles, int W, int chunk) {
+  using V = VecT<VW>;
+  using Tv = typename V::T;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int L = 1 << lshift;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int G = 32 >> lshift;  // sub-warps per warp
+  const int sub = lane >> lshift;
+  const int sl = lane & (L - 1);
+  const unsigned submask = (L == 32) ? 0xffffffffu : (((1u << L) - 1u) << (sub * L));
+  // per warp: 2 buffers x (G*chunk) columns x (1 int + R floats)
+  const int wcols = G * chunk;
+  int *wcol = reinterpret_cast<int *>(smem_raw) + (size_t)warp * 2 * wcols * (R + 1);
+  float *wval = reinterpret_cast<float *>(wcol + 2 * wcols);
+  const int n_short = ROWPTR ? P.n_units : P.n_short;
+  const int n_long = ROWPTR ? 0 : P.n_long;
+  const int n_sg = (n_short + G - 1) / G;
+  const long long per_tile = (long long)n_long + n_sg;
+  const long long n_items = per_tile * n_otiles;
+  const long long nwarps = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long item = (long long)blockIdx.x * (blockDim.x >> 5) + warp; item < n_items;
+       item += nwarps) {
+    const int ot = (int)(item / per_tile);
+    const long long w = item - (long long)ot * per_tile;
+    int4 U;
+    int cg, ncg, t, T, lead;
+    unsigned tmask;
+    int *bcol;
+    float *bval;
+    int chk;
+    if (w < n_long) {  // the whole warp on one long unit
+      U = __ldg(P.units + __ldg(P.long_idx + w));
+      cg = sub; ncg = G; t = lane; T = 32; tmask = 0xffffffffu; lead = 0;
+      bcol = wcol; bval = wval; chk = wcols;
+    } else {  // one short unit per sub-warp
+      const long long s = (w - n_long) * G + sub;
+      if (s >= n_short) {
+        U = make_int4(0, 0, 0, -2);  // idle sub-warp
+      } else if constexpr (ROWPTR) {
+        U = make_int4((int)s, __ldg(P.row_ptr + s), __ldg(P.row_ptr + s + 1), -1);
+      } else {
+        U = __ldg(P.units + __ldg(P.short_idx + s));
+      }
+      cg = 0; ncg = 1; t = sl; T = L; tmask = submask; lead = sub * L;
+      bcol = wcol + sub * chunk * 2;
+      bval = wval + (size_t)sub * chunk * 2 * R;
+      chk = chunk;
+    }
+    if (U.w == -2) continue;
+    int kk[NV];
+    bool ok[NV];
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      kk[v] = ot * W + v * (L * VW) + sl * VW;
+      ok[v] = kk[v] < O;
+    }
+    Tv acc[R][NV];
+    walk_unit<R, NV, VW>(P, B, ldb, U, kk, ok, cg, ncg, t, T, tmask, L, chk, bcol,
+                         bval, acc);
+    finish_unit<R, NV, VW>(P, C, ldc, U, ot, kk, ok, cg, ncg, lead, tmask, acc);
+  }
+}
+
+using KernelFn = void (*)(const PanelDevView, const float *, int, float *, int, int,
                           int, int, int, int);
 
 template <int R, int NV, int VW, bool ROWPTR>
 constexpr KernelFn kfn() {
-  return panel_spmm_kernel<R, NV, VW, (R <= 4 ? 4 : (R == 8 ? 2 : 1)), ROWPTR>;
+  return panel_spmm_kernel<R, NV, VW, ROWPTR>;
 }
 
 KernelFn select_kernel(int R, int NV, int VW, bool rowptr) {
@@ -229,8 +525,8 @@ KernelFn select_kernel(int R, int NV, int VW, bool rowptr) {
     if (NV == 1) return VW == 4 ? kfn<1, 1, 4, true>() : kfn<1, 1, 1, true>();
     return VW == 4 ? kfn<1, 2, 4, true>() : kfn<1, 2, 1, true>();
   }
-#define VCSR_SEL(RR)                                                         \
-  case RR:                                                                   \
+#define VCSR_SEL(RR)                                                              \
+  case RR:                                                                        \
     if (NV == 1) return VW == 4 ? kfn<RR, 1, 4, false>() : kfn<RR, 1, 1, false>(); \
     return VW == 4 ? kfn<RR, 2, 4, false>() : kfn<RR, 2, 1, false>();
   switch (R) {
@@ -279,9 +575,17 @@ LaunchShape pick_shape(int O, int R, bool vec4) {
   return s;
 }
 
-vcsr_status launch_panel_spmm(const PanelDevView &P, bool rowptr,
-                              const float *B, int ldb, float *C, int ldc, int O,
-                              cudaStream_t st, int *launches) {
+// Columns staged per sub-warp per buffer: about 10 KB of shared memory per
+// warp for both buffers, between 4 and 128 columns (a multiple of 4).
+int stage_chunk_cols(int R, int G) {
+  int c = 10240 / (2 * G * (R + 1) * 4);
+  c = c < 4 ? 4 : (c > 128 ? 128 : c);
+  return c & ~3;
+}
+
+vcsr_status launch_panel_spmm(const PanelDevView &P, bool rowptr, const float *B,
+                              int ldb, float *C, int ldc, int O, cudaStream_t st,
+                              int *launches) {
   if (launches) *launches = 0;
   if (O <= 0 || P.n_units <= 0) return VCSR_OK;
   const bool vec4 = (O % 4 == 0) && (ldb % 4 == 0) && (ldc % 4 == 0) &&
@@ -292,16 +596,24 @@ vcsr_status launch_panel_spmm(const PanelDevView &P, bool rowptr,
   if (!rowptr && P.n_split_units > 0 && (O > P.pstride || s.n_otiles > P.counter_stride))
     return fail(VCSR_ERR_INVALID, "O=%d exceeds the plan's max_O=%d", O, P.pstride);
   const int threads = 256;
+  const int G = 32 >> s.lshift;
+  const int chunk = stage_chunk_cols(P.R, G);
+  const size_t smem = (size_t)(threads / 32) * 2 * G * chunk * (P.R + 1) * 4;
+  if (smem > 48 * 1024)
+    VCSR_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)smem));
   int per_sm = 0;
-  VCSR_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, 0));
+  VCSR_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem));
   if (per_sm <= 0) per_sm = 1;
-  const int subs_per_block = (threads / 32) * (32 >> s.lshift);
-  const long long items = (long long)P.n_units * s.n_otiles;
-  long long blocks = (items + subs_per_block - 1) / subs_per_block;
+  const int n_short = rowptr ? P.n_units : P.n_short;
+  const int n_long = rowptr ? 0 : P.n_long;
+  const long long items = ((long long)n_long + (n_short + G - 1) / G) * s.n_otiles;
+  long long blocks = (items + (threads / 32) - 1) / (threads / 32);
   const long long cap = (long long)sm_count() * per_sm;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
-  fn<<<(int)blocks, threads, 0, st>>>(P, B, ldb, C, ldc, O, s.lshift, s.n_otiles, s.W);
+  fn<<<(int)blocks, threads, smem, st>>>(P, B, ldb, C, ldc, O, s.lshift, s.n_otiles, s.W,
+                                         chunk);
   VCSR_CUDA(cudaGetLastError());
   if (launches) *launches = 1;
   return VCSR_OK;
@@ -315,8 +627,7 @@ extern "C" vcsr_status vcsr_csr_spmm(int M, const int *d_row_ptr, const int *d_c
   vcsr::clear_error();
   if (M < 0 || O < 0) return vcsr::fail(VCSR_ERR_INVALID, "negative size");
   if (M == 0 || O == 0) return VCSR_OK;
-  if (!d_row_ptr || !dB || !dC)
-    return vcsr::fail(VCSR_ERR_INVALID, "null device pointer");
+  if (!d_row_ptr || !dB || !dC) return vcsr::fail(VCSR_ERR_INVALID, "null device pointer");
   vcsr::PanelDevView P{};
   P.row_ptr = d_row_ptr;
   P.ucol = d_col;
@@ -324,6 +635,5 @@ extern "C" vcsr_status vcsr_csr_spmm(int M, const int *d_row_ptr, const int *d_c
   P.n_units = M;
   P.M = M;
   P.R = 1;
-  return vcsr::launch_panel_spmm(P, true, dB, O, dC, O, O, (cudaStream_t)stream,
-                                 nullptr);
+  return vcsr::launch_panel_spmm(P, true, dB, O, dC, O, O, (cudaStream_t)stream, nullptr);
 }

@@ -76,7 +76,7 @@ class _PlanInfo(C.Structure):
                 ("vec_rows", C.c_int), ("num_vectors", C.c_int),
                 ("num_union", C.c_int64), ("num_units", C.c_int),
                 ("num_split_vectors", C.c_int), ("num_split_units", C.c_int),
-                ("panel_bytes", C.c_int64), ("has_reference_format", C.c_int),
+                ("num_long_units", C.c_int), ("panel_bytes", C.c_int64), ("has_reference_format", C.c_int),
                 ("build_ms", C.c_double)]
 
 
@@ -123,6 +123,14 @@ _SIGS = {
     "vcsr_partition_rows": (C.c_int, [_i32p, C.c_int, C.c_int, C.c_int, _i32p]),
     "vcsr_csr_row_panel": (C.c_int, [C.POINTER(_Csr), C.c_int, C.c_int,
                                      C.POINTER(_Csr)]),
+    "vcsr_mgpu_create": (C.c_int, [C.POINTER(_Csr), C.c_int, _i32p,
+                                   C.POINTER(_PlanParams), C.POINTER(C.c_void_p)]),
+    "vcsr_mgpu_set_b": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int,
+                                  C.POINTER(C.c_float)]),
+    "vcsr_mgpu_spmm": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_float)]),
+    "vcsr_mgpu_gather_c": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "vcsr_mgpu_cuts": (C.c_int, [C.c_void_p, _i32p]),
+    "vcsr_mgpu_destroy": (None, [C.c_void_p]),
 }
 
 
@@ -469,6 +477,57 @@ class Plan:
     def close(self):
         if getattr(self, "_h", None):
             lib().vcsr_plan_destroy(self._h)
+            self._h = None
+
+    __del__ = close
+
+
+class MultiGPU:
+    """Row panels of A on several GPUs of this process (vcsr_mgpu_*): one plan
+    per GPU, B replicated by one NCCL broadcast, disjoint C panels."""
+
+    def __init__(self, csr: CSR, ngpus, devices=None, segw=4, bundle=32, max_O=512,
+                 vec_rows=0):
+        L = lib()
+        p = _PlanParams()
+        L.vcsr_plan_params_default(C.byref(p))
+        p.segw, p.bundle, p.max_O, p.vec_rows = segw, bundle, max_O, vec_rows
+        s = csr._struct()
+        devs = None
+        if devices is not None:
+            self._devs = np.ascontiguousarray(devices, np.int32)
+            devs = self._devs.ctypes.data_as(_i32p)
+        h = C.c_void_p()
+        _check(L.vcsr_mgpu_create(C.byref(s), ngpus, devs, C.byref(p), C.byref(h)))
+        self._h = h
+        self.n = ngpus
+        self.M, self.N = csr.M, csr.N
+
+    def cuts(self):
+        c = np.zeros(self.n + 1, np.int32)
+        _check(lib().vcsr_mgpu_cuts(self._h, c.ctypes.data_as(_i32p)))
+        return c
+
+    def set_b(self, hB):
+        hB = np.ascontiguousarray(hB, np.float32)
+        ms = C.c_float()
+        _check(lib().vcsr_mgpu_set_b(self._h, hB.ctypes.data, hB.shape[1], C.byref(ms)))
+        self.O = hB.shape[1]
+        return ms.value
+
+    def spmm(self):
+        ms = C.c_float()
+        _check(lib().vcsr_mgpu_spmm(self._h, self.O, C.byref(ms)))
+        return ms.value
+
+    def gather_c(self):
+        out = np.empty((self.M, self.O), np.float32)
+        _check(lib().vcsr_mgpu_gather_c(self._h, out.ctypes.data))
+        return out
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().vcsr_mgpu_destroy(self._h)
             self._h = None
 
     __del__ = close
