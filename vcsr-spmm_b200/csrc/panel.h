@@ -53,8 +53,8 @@ struct PanelHost {
   std::vector<SplitVec> svecs;
 };
 
-// Union size per candidate R on a sample of vectors, and the R the cost
-// model picks (cost per union column ~ one B-row load + R FMA issues).
+// Union sizes per candidate R on a sample of 16-row windows; returns the
+// largest R <= 8 whose vectors are at least 60% dense.
 int choose_vec_rows(const vcsr_csr &csr, double *density_out);
 
 // Build the layout on the host for a given R (1, 2, 4, 8, 16).  chunk <= 0

@@ -61,17 +61,16 @@ int choose_vec_rows(const vcsr_csr &csr, double *density_out) {
 #pragma omp critical
     for (int ci = 0; ci < 5; ++ci) unions[ci] += loc[ci];
   }
+  // The largest R (up to 8) whose vectors are still at least 60% dense:
+  // measured on B200, a denser vector trades one B-row load for more FMAs per
+  // union column, while below ~60% density the padded FMAs cost more than the
+  // saved loads.  R = 16 is never picked automatically (its 64 float
+  // accumulators per lane halve occupancy); callers may still ask for it.
   int best = 1;
-  double best_cost = 0;
-  for (int ci = 0; ci < 5; ++ci) {
+  for (int ci = 1; ci < 4; ++ci) {
     const int R = cands[ci];
-    // per union column: one B-row load (~5 issue slots incl. index and value
-    // loads) plus R FMA issues and R/4 value loads
-    const double cost = unions[ci] * (5.0 + 1.25 * R);
-    if (ci == 0 || cost < best_cost * 0.97) {
-      best = R;
-      best_cost = cost;
-    }
+    const double dens = unions[ci] > 0 ? (double)nnz_s / (unions[ci] * R) : 0.0;
+    if (dens >= 0.6) best = R;
   }
   if (density_out) {
     int ci = 0;

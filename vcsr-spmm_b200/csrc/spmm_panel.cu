@@ -144,20 +144,31 @@ __device__ __forceinline__ void load_vals_smem(const float *sval, int j, float (
 
 // Columns per prefetch group: B loads of group g+1 are in flight while
 // group g is consumed, so a lane holds 2 * UN * NV 128-bit B values.
-// Build-time tuning knobs (defaults measured on B200, see the design notes).
-#ifndef VCSR_UN_SMALL_R
-#define VCSR_UN_SMALL_R 8  // R <= 4, NV = 1
-#endif
-#ifndef VCSR_UN_R8
-#define VCSR_UN_R8 4       // R = 8, NV = 1
-#endif
-#ifndef VCSR_PANEL_MIN_BLOCKS
-#define VCSR_PANEL_MIN_BLOCKS 1
-#endif
-template <int R, int NV>
+// Per-instantiation tuning, measured on B200 (tests of unroll depth and
+// register caps over the five workloads): UN = columns per prefetch group
+// (two groups in flight), MINB = blocks of 256 threads that must fit on an
+// SM (caps registers at 65536 / (256 * MINB)).  VCSR_TUNE_UN / _MINB override
+// both for experiments.
+template <int R, int NV, int VW>
 constexpr int unroll_for() {
-  return R <= 4 ? (NV == 1 ? VCSR_UN_SMALL_R : VCSR_UN_SMALL_R / 2)
-                : (R == 8 ? (NV == 1 ? VCSR_UN_R8 : VCSR_UN_R8 / 2) : 2);
+#ifdef VCSR_TUNE_UN
+  return VCSR_TUNE_UN;
+#else
+  if (VW == 1) return R <= 4 ? (NV == 1 ? 8 : 4) : (R == 8 ? (NV == 1 ? 4 : 2) : 2);
+  if (R <= 4) return NV == 1 ? 4 : (R == 4 ? 2 : (R == 2 ? 4 : 2));
+  return 2 + (R == 8 && NV == 1 ? 2 : 0);
+#endif
+}
+template <int R, int NV, int VW>
+constexpr int min_blocks_for() {
+#ifdef VCSR_TUNE_MINB
+  return VCSR_TUNE_MINB;
+#else
+  if (VW == 1) return 1;
+  if (R <= 4) return NV == 1 ? 3 : (R == 1 ? 4 : 2);
+  if (R == 8) return NV == 1 ? 2 : 1;
+  return 2;
+#endif
 }
 
 // Accumulators.  With 128-bit lanes the sums are kept as float2 pairs so that
@@ -291,7 +302,7 @@ __device__ __forceinline__ void walk_unit(
     typename VecT<VW>::T (&out)[R][NV]) {
   using V = VecT<VW>;
   using Tv = typename V::T;
-  constexpr int UN = unroll_for<R, NV>();
+  constexpr int UN = unroll_for<R, NV, VW>();
   Acc<R, NV, VW> acc;
   acc.zero();
   const float *Bk = B + kk[0];
@@ -445,7 +456,7 @@ __device__ __forceinline__ void finish_unit(
 }
 
 template <int R, int NV, int VW, bool ROWPTR>
-__global__ void __launch_bounds__(256, VCSR_PANEL_MIN_BLOCKS)
+__global__ void __launch_bounds__(256, (min_blocks_for<R, NV, VW>()))
     panel_spmm_kernel(const PanelDevView P, const float *__restrict__ B, int ldb,
                       float *__restrict__ C, int ldc, int O, int lshift,
                       int n_otiles, int W, int chunk) {
