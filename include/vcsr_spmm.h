@@ -223,6 +223,34 @@ vcsr_status vcsr_csr_spmm(int M, const int *d_row_ptr, const int *d_col,
                           const float *d_val, const float *dB, int O,
                           float *dC, vcsr_stream_t stream);
 
+/* CSR SpMM that allocates nothing (no cudaMalloc, cudaFree or allocating
+ * library call).  No counterpart in the reference.  For callers that cannot
+ * allocate device memory: a solver embedded in an application whose framework
+ * hands all free device memory to its own caching pool at start-up (a
+ * cudaMalloc would then fail, or take memory the pool counts on), or a code
+ * path that has a fixed device-memory budget.  Same contract as vcsr_csr_spmm
+ * (C = A*B, ld = O, device pointers), but rows longer than
+ * VCSR_NOALLOC_SPLIT entries are cut into parts walked by separate warps, and
+ * the bookkeeping and partial sums of those parts live in one
+ * VCSR_NOALLOC_SCRATCH_BYTES array compiled into the library (every GPU that
+ * loads the library holds it until the process exits).  Limits, rejected
+ * with VCSR_ERR_RANGE and a message: O <= VCSR_NOALLOC_MAX_O; at most
+ * VCSR_NOALLOC_MAX_LONG_ROWS long rows; at most VCSR_NOALLOC_MAX_PARTS parts
+ * over all long rows (the last two are detected on the device, and C is then
+ * incomplete).  The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call
+ * before any stream capture.  Each call clears the counters it needs,
+ * synchronises `stream` once to read the overflow flag, and shares the one
+ * array: calls that overlap on the GPU (other streams, other threads) race. */
+#define VCSR_NOALLOC_MAX_O 512
+#define VCSR_NOALLOC_MAX_LONG_ROWS 1024
+#define VCSR_NOALLOC_MAX_PARTS 2048
+#define VCSR_NOALLOC_SPLIT 4096
+#define VCSR_NOALLOC_SCRATCH_BYTES 6320384
+vcsr_status vcsr_csr_spmm_noalloc(int M, const int *d_row_ptr, const int *d_col,
+                                  const float *d_val, const float *dB, int O,
+                                  float *dC, vcsr_stream_t stream);
+
 /* cuSPARSE SpMM with the handle, descriptors, buffer and preprocessing made
  * once; replaces run_cusparse_spmm (src/kernels.cu:170-235).  alg: 0 =
  * CUSPARSE_SPMM_ALG_DEFAULT, 1 = CSR_ALG1, 2 = CSR_ALG2, 3 = CSR_ALG3. */

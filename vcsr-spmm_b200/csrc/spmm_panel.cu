@@ -648,3 +648,230 @@ extern "C" vcsr_status vcsr_csr_spmm(int M, const int *d_row_ptr, const int *d_c
   P.R = 1;
   return vcsr::launch_panel_spmm(P, true, dB, O, dC, O, O, (cudaStream_t)stream, nullptr);
 }
+
+// ------------------------------------------------- allocation-free CSR SpMM
+//
+// vcsr_csr_spmm_noalloc is the CSR row-wise SpMM above with long rows split
+// over several warps, for callers that may not allocate device memory.  The
+// split needs scratch (which rows are long, their part bookkeeping, the
+// partial sums and the last-part tickets); here it lives in one file-scope
+// __device__ array instead of memory the library would allocate.  Nothing in
+// the reference corresponds to it.
+namespace vcsr {
+namespace noalloc {
+
+constexpr int kMaxO = VCSR_NOALLOC_MAX_O;
+constexpr int kMaxLong = VCSR_NOALLOC_MAX_LONG_ROWS;
+constexpr int kMaxParts = VCSR_NOALLOC_MAX_PARTS;
+constexpr int kSplit = VCSR_NOALLOC_SPLIT;
+constexpr size_t round256(size_t x) { return (x + 255) & ~(size_t)255; }
+// ctrl[0] long rows found, ctrl[1] error bits, ctrl[2] parts reserved
+constexpr size_t kCtrl = 0;
+constexpr size_t kLong = 256;                                    // int[kMaxLong]
+constexpr size_t kSvec = round256(kLong + 4 * (size_t)kMaxLong);   // int2[kMaxLong]
+constexpr size_t kParts = round256(kSvec + 8 * (size_t)kMaxLong);  // int2[kMaxParts]
+constexpr size_t kTickets = round256(kParts + 8 * (size_t)kMaxParts);  // int[kMaxLong*kMaxO]
+constexpr size_t kPartials =
+    round256(kTickets + 4 * (size_t)kMaxLong * kMaxO);           // float[kMaxParts*kMaxO]
+constexpr size_t kBytes = kPartials + 4 * (size_t)kMaxParts * kMaxO;
+static_assert(kBytes == VCSR_NOALLOC_SCRATCH_BYTES, "header and layout disagree");
+
+}  // namespace noalloc
+}  // namespace vcsr
+
+// The scratch.  In host code this name is only a handle for the runtime;
+// kernels get its device address from cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[vcsr::noalloc::kBytes];
+
+namespace vcsr {
+namespace {
+
+// Rows longer than kSplit entries get a slot, a range of part slots and
+// their {slot, part} records; overflow sets an error bit and skips the row.
+__global__ void noalloc_classify_kernel(const int *__restrict__ rp, int M,
+                                        unsigned char *S) {
+  using namespace noalloc;
+  int *ctrl = reinterpret_cast<int *>(S + kCtrl);
+  int *lr = reinterpret_cast<int *>(S + kLong);
+  int2 *sv = reinterpret_cast<int2 *>(S + kSvec);
+  int2 *parts = reinterpret_cast<int2 *>(S + kParts);
+  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < M; r += gridDim.x * blockDim.x) {
+    const int len = rp[r + 1] - rp[r];
+    if (len <= kSplit) continue;
+    const int np = (len + kSplit - 1) / kSplit;
+    const int s = atomicAdd(&ctrl[0], 1);
+    if (s >= kMaxLong) {
+      atomicOr(&ctrl[1], 1);
+      continue;
+    }
+    const int base = atomicAdd(&ctrl[2], np);
+    if (base + np > kMaxParts) {
+      atomicOr(&ctrl[1], 2);
+      lr[s] = -1;
+      continue;
+    }
+    lr[s] = r;
+    sv[s] = make_int2(base, np);
+    for (int p = 0; p < np; ++p) parts[base + p] = make_int2(s, p);
+  }
+}
+
+// Short rows: one sub-warp per row, exactly as vcsr_csr_spmm.  Long rows:
+// one warp per (part, O-tile); the parts are added by the last one to finish.
+template <int NV, int VW>
+__global__ void __launch_bounds__(256, (min_blocks_for<1, NV, VW>()))
+    noalloc_spmm_kernel(const int *__restrict__ rp, const int *__restrict__ col,
+                        const float *__restrict__ val, int M,
+                        const float *__restrict__ B, int ldb, float *__restrict__ C,
+                        int ldc, int O, int lshift, int n_otiles, int W, int chunk,
+                        unsigned char *S) {
+  using namespace noalloc;
+  using Tv = typename VecT<VW>::T;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int *ctrl = reinterpret_cast<const int *>(S + kCtrl);
+  const int *lr = reinterpret_cast<const int *>(S + kLong);
+  PanelDevView P{};
+  P.ucol = col;
+  P.uval = val;
+  P.M = M;
+  P.R = 1;
+  P.parts = reinterpret_cast<const int2 *>(S + kParts);
+  P.svecs = reinterpret_cast<const int2 *>(S + kSvec);
+  P.partials = reinterpret_cast<float *>(S + kPartials);
+  P.counters = reinterpret_cast<int *>(S + kTickets);
+  P.pstride = O;
+  P.counter_stride = n_otiles;
+  const int L = 1 << lshift;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int G = 32 >> lshift, sub = lane >> lshift, sl = lane & (L - 1);
+  const unsigned submask = (L == 32) ? 0xffffffffu : (((1u << L) - 1u) << (sub * L));
+  const int wcols = G * chunk;
+  int *wcol = reinterpret_cast<int *>(smem_raw) + (size_t)warp * 2 * wcols * 2;
+  float *wval = reinterpret_cast<float *>(wcol + 2 * wcols);
+  const int n_parts = min(ctrl[2], kMaxParts);
+  const long long n_sg = (M + G - 1) / G;
+  const long long per_tile = n_parts + n_sg;
+  const long long n_items = per_tile * n_otiles;
+  const long long nwarps = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long item = (long long)blockIdx.x * (blockDim.x >> 5) + warp; item < n_items;
+       item += nwarps) {
+    const int ot = (int)(item / per_tile);
+    const long long w = item - (long long)ot * per_tile;
+    int4 U;
+    int cg, ncg, t, T, lead, chk;
+    unsigned tmask;
+    int *bcol;
+    float *bval;
+    if (w < n_parts) {  // one part of a long row, whole warp
+      const int2 sp = P.parts[w];
+      const int r = sp.x >= 0 ? lr[sp.x] : -1;
+      if (r < 0) continue;
+      const int b = rp[r] + sp.y * kSplit;
+      U = make_int4(r, b, min(b + kSplit, rp[r + 1]), (int)w);
+      cg = sub; ncg = G; t = lane; T = 32; tmask = 0xffffffffu; lead = 0;
+      bcol = wcol; bval = wval; chk = wcols;
+    } else {
+      const long long r = (w - n_parts) * G + sub;
+      if (r >= M) {
+        U = make_int4(0, 0, 0, -2);
+      } else {
+        const int b = rp[r], e = rp[r + 1];
+        U = (e - b > kSplit) ? make_int4(0, 0, 0, -2) : make_int4((int)r, b, e, -1);
+      }
+      cg = 0; ncg = 1; t = sl; T = L; tmask = submask; lead = sub * L;
+      bcol = wcol + sub * chunk * 2;
+      bval = wval + (size_t)sub * chunk * 2;
+      chk = chunk;
+    }
+    if (U.w == -2) continue;
+    int kk[NV];
+    bool ok[NV];
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      kk[v] = ot * W + v * (L * VW) + sl * VW;
+      ok[v] = kk[v] < O;
+    }
+    Tv acc[1][NV];
+    walk_unit<1, NV, VW>(P, B, ldb, U, kk, ok, cg, ncg, t, T, tmask, L, chk, bcol, bval, acc);
+    finish_unit<1, NV, VW>(P, C, ldc, U, ot, kk, ok, cg, ncg, lead, tmask, acc);
+  }
+}
+
+std::mutex g_noalloc_mu;
+unsigned char *g_noalloc_ptr[64] = {};
+
+// Device address of the scratch on the current device (set up once per
+// device, with that device current).
+vcsr_status noalloc_scratch(unsigned char **out) {
+  int dev = 0;
+  VCSR_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(VCSR_ERR_UNSUPPORTED, "device ordinal %d >= 64", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void *p = nullptr;
+    VCSR_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    g_noalloc_ptr[dev] = static_cast<unsigned char *>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return VCSR_OK;
+}
+
+}  // namespace
+}  // namespace vcsr
+
+extern "C" vcsr_status vcsr_csr_spmm_noalloc(int M, const int *d_row_ptr,
+                                             const int *d_col, const float *d_val,
+                                             const float *dB, int O, float *dC,
+                                             vcsr_stream_t stream) {
+  using namespace vcsr;
+  using namespace vcsr::noalloc;
+  clear_error();
+  if (M < 0 || O < 0) return fail(VCSR_ERR_INVALID, "negative size");
+  if (O > kMaxO)
+    return fail(VCSR_ERR_RANGE, "O = %d exceeds the allocation-free limit of %d columns",
+                O, kMaxO);
+  if (M == 0 || O == 0) return VCSR_OK;
+  if (!d_row_ptr || !dB || !dC) return fail(VCSR_ERR_INVALID, "null device pointer");
+  unsigned char *S = nullptr;
+  VCSR_TRY(noalloc_scratch(&S));
+  cudaStream_t st = (cudaStream_t)stream;
+  // the counters, the part records and every ticket must start at zero / -1
+  VCSR_CUDA(cudaMemsetAsync(S + kCtrl, 0, 256, st));
+  VCSR_CUDA(cudaMemsetAsync(S + kParts, 0xff, 8 * (size_t)kMaxParts, st));
+  VCSR_CUDA(cudaMemsetAsync(S + kTickets, 0, 4 * (size_t)kMaxLong * kMaxO, st));
+  const int sms = sm_count();
+  noalloc_classify_kernel<<<sms * 4, 256, 0, st>>>(d_row_ptr, M, S);
+  VCSR_CUDA(cudaGetLastError());
+  const bool vec4 = (O % 4 == 0) && ((uintptr_t)dB % 16 == 0) && ((uintptr_t)dC % 16 == 0);
+  const LaunchShape s = pick_shape(O, 1, vec4);
+  using Fn = void (*)(const int *, const int *, const float *, int, const float *, int,
+                      float *, int, int, int, int, int, int, unsigned char *);
+  Fn fn = s.VW == 4 ? (s.NV == 1 ? (Fn)noalloc_spmm_kernel<1, 4> : (Fn)noalloc_spmm_kernel<2, 4>)
+                    : (s.NV == 1 ? (Fn)noalloc_spmm_kernel<1, 1> : (Fn)noalloc_spmm_kernel<2, 1>);
+  const int threads = 256, G = 32 >> s.lshift;
+  const int chunk = stage_chunk_cols(1, G);
+  const size_t smem = (size_t)(threads / 32) * 2 * G * chunk * 2 * 4;
+  if (smem > 48 * 1024)
+    VCSR_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  int per_sm = 0;
+  VCSR_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem));
+  const long long items = ((long long)kMaxParts + (M + G - 1) / G) * s.n_otiles;
+  long long blocks = (items + (threads / 32) - 1) / (threads / 32);
+  const long long cap = (long long)sms * (per_sm > 0 ? per_sm : 1);
+  blocks = blocks > cap ? cap : (blocks < 1 ? 1 : blocks);
+  fn<<<(int)blocks, threads, smem, st>>>(d_row_ptr, d_col, d_val, M, dB, O, dC, O, O,
+                                         s.lshift, s.n_otiles, s.W, chunk, S);
+  VCSR_CUDA(cudaGetLastError());
+  int err = 0;
+  VCSR_CUDA(cudaMemcpyAsync(&err, S + kCtrl + 4, sizeof(int), cudaMemcpyDeviceToHost, st));
+  VCSR_CUDA(cudaStreamSynchronize(st));
+  if (err & 1)
+    return fail(VCSR_ERR_RANGE,
+                "more than %d rows longer than %d entries: exceeds the allocation-free "
+                "scratch (C is incomplete)", kMaxLong, kSplit);
+  if (err & 2)
+    return fail(VCSR_ERR_RANGE,
+                "long rows need more than %d parts of %d entries: exceeds the "
+                "allocation-free scratch (C is incomplete)", kMaxParts, kSplit);
+  return VCSR_OK;
+}

@@ -114,6 +114,8 @@ _SIGS = {
                                       C.c_void_p, C.c_void_p]),
     "vcsr_csr_spmm": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
                                 C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
+    "vcsr_csr_spmm_noalloc": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                        C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
     "vcsr_cusparse_create": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_void_p,
                                        C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
                                        C.c_void_p, C.c_int, C.c_void_p,
@@ -398,6 +400,14 @@ def run_csr_spmm_gpu(M, d_rowptr, d_col, d_val, dB, O, dC, stream=None):
     """run_csr_spmm_gpu (src/kernels.cu:107): C = A*B."""
     _check(lib().vcsr_csr_spmm(M, _ptr(d_rowptr), _ptr(d_col), _ptr(d_val),
                                _ptr(dB), O, _ptr(dC), _stream(stream)))
+
+
+def csr_spmm_noalloc(M, d_rowptr, d_col, d_val, dB, O, dC, stream=None):
+    """C = A*B like run_csr_spmm_gpu, without allocating device memory: the
+    scratch for split long rows is a fixed array inside the library
+    (vcsr_csr_spmm_noalloc).  Synchronises the stream."""
+    _check(lib().vcsr_csr_spmm_noalloc(M, _ptr(d_rowptr), _ptr(d_col), _ptr(d_val),
+                                       _ptr(dB), O, _ptr(dC), _stream(stream)))
 
 
 class CuSparse:
