@@ -51,7 +51,7 @@ WORKLOADS = {
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="fem")
@@ -90,52 +90,79 @@ def profile_traffic(label):
 
 
 class Clocks:
-    """SM clock and clock-event reasons sampled through NVML every ~0.5 ms in
-    a background thread while the timed region runs."""
+    """SM clock and clock-event reasons of one GPU, sampled through NVML by a
+    child process (so the benchmark's own thread never delays it) as fast as
+    NVML answers; only samples inside [start, stop] count (or the one just
+    before start, when the timed region is shorter than a sample)."""
+    CHILD = r"""
+import sys, time
+import pynvml as N
+N.nvmlInit()
+h = N.nvmlDeviceGetHandleByUUID(sys.argv[1])
+print("max", N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM), flush=True)
+import select
+while True:
+    r, _, _ = select.select([sys.stdin], [], [], 0)
+    if r and not sys.stdin.readline():
+        break
+    t = time.monotonic()
+    c = N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM)
+    e = N.nvmlDeviceGetCurrentClocksEventReasons(h)
+    print(f"{t:.6f} {c} {e}", flush=False)
+sys.stdout.flush()
+"""
     REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
                0x40: "hw_thermal_slowdown"}
 
     def __init__(self, uuid):
         self.uuid = uuid
-        self.samples = []
-        self.reasons = 0
-        self.thread = None
-        self.stop_flag = False
+        self.proc = None
+        self.t0 = self.t1 = None
         self.max_mhz = None
 
-    def start(self):
-        import threading
+    def launch(self):
+        import subprocess
         try:
-            import pynvml as N
-            N.nvmlInit()
-            h = N.nvmlDeviceGetHandleByUUID(self.uuid)
-            self.max_mhz = float(N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM))
+            self.proc = subprocess.Popen([sys.executable, "-c", self.CHILD, self.uuid],
+                                         stdin=subprocess.PIPE, stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            first = self.proc.stdout.readline().split()
+            self.max_mhz = float(first[1]) if len(first) == 2 else None
         except Exception:
-            self.thread = None
-            return
+            self.proc = None
 
-        def loop():
-            while not self.stop_flag:
-                try:
-                    self.samples.append(float(N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM)))
-                    self.reasons |= int(N.nvmlDeviceGetCurrentClocksEventReasons(h))
-                except Exception:
-                    pass
-                time.sleep(0.0005)
-
-        self.thread = threading.Thread(target=loop, daemon=True)
-        self.thread.start()
+    def start(self):
+        self.t0 = time.monotonic()
 
     def stop(self):
-        if self.thread is None:
+        self.t1 = time.monotonic()
+        if self.proc is None:
             return None
-        self.stop_flag = True
-        self.thread.join(timeout=5)
-        if not self.samples:
+        time.sleep(0.002)
+        try:
+            out, _ = self.proc.communicate(input="\n", timeout=30)
+        except Exception:
+            self.proc.kill()
             return None
-        return {"sm_mhz": float(np.median(self.samples)), "sm_max_mhz": self.max_mhz,
-                "reasons": sorted(v for k, v in self.REASONS.items() if self.reasons & k),
-                "samples": len(self.samples), "source": "nvml"}
+        samples = []
+        for line in out.splitlines():
+            f = line.split()
+            if len(f) == 3:
+                samples.append((float(f[0]), float(f[1]), int(f[2])))
+        inside = [x for x in samples if self.t0 <= x[0] <= self.t1]
+        if not inside:
+            before = [x for x in samples if x[0] < self.t0]
+            inside = before[-1:]
+        if not inside:
+            return None
+        reasons = 0
+        for x in inside:
+            reasons |= x[2]
+        return {"sm_mhz": float(np.median([x[1] for x in inside])),
+                "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(v for k, v in self.REASONS.items() if reasons & k),
+                "samples": len(inside), "source": "nvml",
+                "window_ms": round((self.t1 - self.t0) * 1e3, 3)}
 
 
 def algorithmic_bytes(csr, O):
@@ -173,17 +200,10 @@ def cpu_reference(csr, B, seconds, min_reps=3):
 
 
 def build_inputs(args, rank, world):
-    import vcsr_b200 as V
+    from vcsr_b200 import dist as D
     cfg, size, O, scaling, label = WORKLOADS[args.workload]
-    full = V.gen_csr(cfg, args.seed + (rank if scaling == "weak" else 0), size)
-    if scaling == "strong" and world > 1:
-        cuts = V.partition_rows(full.row_ptr, world, 16)
-        csr = V.csr_row_panel(full, int(cuts[rank]), int(cuts[rank + 1]))
-        global_nnz = full.nnz
-    else:
-        csr = full
-        global_nnz = full.nnz * world
-    return csr, O, scaling, label, global_nnz
+    csr, row0, total = D.rank_panel(cfg, size, args.seed, rank, world, scaling, align=16)
+    return csr, O, scaling, label, total
 
 
 def run_reference(args):
@@ -236,7 +256,10 @@ def run_ours(args):
                                 device_id=dev)
     stream = torch.cuda.current_stream()
 
-    csr, O, scaling, label, global_nnz = build_inputs(args, rank, world)
+    from vcsr_b200 import dist as D
+    csr, O, scaling, label, strong_total = build_inputs(args, rank, world)
+    global_nnz = D.global_nnz(csr, scaling, world, strong_total,
+                              dist if world > 1 else None, dev)
     lo = 0.0 if WORKLOADS[args.workload][0] == "rmat" else -1.0
     plan = V.Plan(csr, segw=4, bundle=32, max_O=max(O, 512))
     info = plan.info()
@@ -251,18 +274,23 @@ def run_ours(args):
         dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        dist.broadcast(dB, src=0)
+        D.broadcast_b(dist, dB, 0)
         e1.record(stream)
         torch.cuda.synchronize()
-        t = torch.tensor([e0.elapsed_time(e1)], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        bcast_ms = float(t.item())
+        bcast_ms = D.max_over_ranks(dist, e0.elapsed_time(e1), dev)
     dC = torch.empty(csr.M, O, device=dev)
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)  # 256 MB
 
     def step():
         plan.spmm(dB, dC, stream=stream)
 
+    try:
+        uuid = str(torch.cuda.get_device_properties(dev).uuid)
+        gpu_id = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+    except Exception:
+        gpu_id = ""
+    clocks = Clocks(gpu_id)
+    clocks.launch()
     for _ in range(args.warmup):
         flush.zero_()
         step()
@@ -270,12 +298,6 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    try:
-        uuid = str(torch.cuda.get_device_properties(dev).uuid)
-        gpu_id = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
-    except Exception:
-        gpu_id = ""
-    clocks = Clocks(gpu_id)
     clocks.start()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -292,12 +314,9 @@ def run_ours(args):
     torch.cuda.synchronize()
     clk = clocks.stop()
     per = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    t_ms = torch.tensor([sum(per)], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t_ms, op=dist.ReduceOp.MAX)
-    total_ms = float(t_ms.item())
+    total_ms = D.max_over_ranks(dist, sum(per), dev) if world > 1 else sum(per)
     ms_step = total_ms / args.steps
-    flops_step = 2.0 * global_nnz * O if scaling == "weak" else 2.0 * global_nnz * O
+    flops_step = 2.0 * global_nnz * O
     value = flops_step / (ms_step * 1e-3) / 1e9
 
     # roofline of the dominant (only) kernel, per launch, on this rank

@@ -31,8 +31,9 @@ struct vcsr_plan {
   int *d_ucol = nullptr;
   float *d_uval = nullptr;
   int4 *d_units = nullptr;
-  int *d_short = nullptr, *d_long = nullptr;
-  int n_short = 0, n_long = 0;
+  int4 *d_batches = nullptr;
+  int *d_long = nullptr, *d_vec_ptr = nullptr;
+  int n_batches = 0, n_long = 0;
   int2 *d_parts = nullptr;
   int2 *d_svecs = nullptr;
   float *d_partials = nullptr;
@@ -42,6 +43,9 @@ struct vcsr_plan {
   // optional segment-major VCSR (include/vcsr.hpp:12-23 layout)
   bool has_ref = false;
   vcsr_vcsr ref{};
+  // side stream and events for running long units beside short ones
+  cudaStream_t side = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
   // host-buffer entry point staging
   float *d_stage_B = nullptr, *d_stage_C = nullptr;
   size_t stage_B = 0, stage_C = 0;
@@ -64,10 +68,13 @@ vcsr_status upload(T **dst, const std::vector<T> &src, cudaStream_t st,
 
 void release(vcsr_plan *p) {
   cudaFree(p->d_ucol); cudaFree(p->d_uval); cudaFree(p->d_units);
-  cudaFree(p->d_short); cudaFree(p->d_long);
+  cudaFree(p->d_batches); cudaFree(p->d_long); cudaFree(p->d_vec_ptr);
   cudaFree(p->d_parts); cudaFree(p->d_svecs); cudaFree(p->d_partials);
   cudaFree(p->d_counters); cudaFree(p->d_stage_B); cudaFree(p->d_stage_C);
   if (p->has_ref) vcsr_vcsr_free(&p->ref, VCSR_DEVICE);
+  if (p->side) cudaStreamDestroy(p->side);
+  if (p->fork) cudaEventDestroy(p->fork);
+  if (p->join) cudaEventDestroy(p->join);
 }
 
 vcsr::PanelDevView view(const vcsr_plan *p) {
@@ -76,8 +83,9 @@ vcsr::PanelDevView view(const vcsr_plan *p) {
   v.uval = p->d_uval;
   v.units = p->d_units;
   v.n_units = p->n_units;
-  v.short_idx = p->d_short;
-  v.n_short = p->n_short;
+  v.batches = p->d_batches;
+  v.n_batches = p->n_batches;
+  v.vec_ptr = p->d_vec_ptr;
   v.long_idx = p->d_long;
   v.n_long = p->n_long;
   v.parts = p->d_parts;
@@ -244,14 +252,44 @@ vcsr_status vcsr_plan_create(const vcsr_csr *csr, int csr_where,
   static_assert(sizeof(vcsr::SplitVec) == sizeof(int2), "SplitVec must match int2");
   std::vector<int4> units(ph.units.size());
   std::memcpy(units.data(), ph.units.data(), sizeof(int4) * units.size());
-  // units of at least kLongUnit union columns are walked by a whole warp
-  // (its sub-warps split the columns); the rest by one sub-warp each
-  constexpr int kLongUnit = 128;
-  std::vector<int> short_idx, long_idx;
-  for (size_t u = 0; u < ph.units.size(); ++u)
-    (ph.units[u].end - ph.units[u].begin >= kLongUnit ? long_idx : short_idx)
-        .push_back((int)u);
-  p->n_short = (int)short_idx.size();
+  // Split parts and units of at least kLongUnit union columns are walked by a
+  // whole warp (its sub-warps split the columns).  The other vectors are
+  // packed, in order, into batches of consecutive vectors walked by one
+  // sub-warp each; a batch holds at most 64 vectors and about `batch_cols`
+  // union columns, chosen so that there are ~64 batches per SM.  With R > 2
+  // a batch is one vector (vectors are long enough on their own).
+  constexpr int kLongUnit = 128, kMaxBatchVecs = 64;
+  std::vector<int> long_idx;
+  std::vector<int4> batches;
+  int64_t short_cols = 0;
+  for (const auto &u : ph.units)
+    if (u.slot < 0 && u.end - u.begin < kLongUnit) short_cols += u.end - u.begin;
+  const int64_t batch_cols =
+      std::max<int64_t>(16, std::min<int64_t>(256, short_cols / ((int64_t)sms * 64)));
+  {
+    int4 cur = make_int4(-1, -1, 0, 0);
+    auto close = [&]() {
+      if (cur.x >= 0) batches.push_back(cur);
+      cur.x = -1;
+    };
+    for (size_t u = 0; u < ph.units.size(); ++u) {
+      const auto &un = ph.units[u];
+      const int len = un.end - un.begin;
+      if (un.slot >= 0 || len >= kLongUnit) {
+        long_idx.push_back((int)u);
+        close();
+        continue;
+      }
+      if (cur.x >= 0 && (ph.R > 2 || cur.w - cur.z + len > batch_cols ||
+                         cur.y - cur.x >= kMaxBatchVecs))
+        close();
+      if (cur.x < 0) cur = make_int4(un.vec, un.vec, un.begin, un.begin);
+      cur.y = un.vec + 1;
+      cur.w = un.end;
+    }
+    close();
+  }
+  p->n_batches = (int)batches.size();
   p->n_long = (int)long_idx.size();
   std::vector<int2> parts(ph.parts.size()), svecs(ph.svecs.size());
   std::memcpy(parts.data(), ph.parts.data(), sizeof(int2) * parts.size());
@@ -261,12 +299,24 @@ vcsr_status vcsr_plan_create(const vcsr_csr *csr, int csr_where,
       (s = upload(&p->d_units, units, st, &p->panel_bytes)) ||
       (s = upload(&p->d_parts, parts, st, &p->panel_bytes)) ||
       (s = upload(&p->d_svecs, svecs, st, &p->panel_bytes)) ||
-      (s = upload(&p->d_short, short_idx, st, &p->panel_bytes)) ||
-      (s = upload(&p->d_long, long_idx, st, &p->panel_bytes))) {
+      (s = upload(&p->d_batches, batches, st, &p->panel_bytes)) ||
+      (s = upload(&p->d_long, long_idx, st, &p->panel_bytes)) ||
+      (s = upload(&p->d_vec_ptr, ph.vec_ptr, st, &p->panel_bytes))) {
     if (owned) vcsr_csr_free(&h, VCSR_HOST);
     release(p);
     delete p;
     return s;
+  }
+  if (p->n_long > 0 && p->n_batches > 0) {
+    cudaError_t e = cudaStreamCreateWithFlags(&p->side, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->fork, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->join, cudaEventDisableTiming);
+    if (e != cudaSuccess) {
+      if (owned) vcsr_csr_free(&h, VCSR_HOST);
+      release(p);
+      delete p;
+      return fail(VCSR_ERR_CUDA, "side stream: %s", cudaGetErrorString(e));
+    }
   }
   if (p->n_split_units > 0) {
     const size_t pbytes = sizeof(float) * (size_t)p->n_split_units * p->R * p->pstride;
@@ -358,7 +408,7 @@ vcsr_status vcsr_spmm(const vcsr_plan *p, const float *dB, int ldb, float *dC,
                 "O=%d exceeds the plan's max_O=%d (split rows need scratch)", O,
                 p->pstride);
   return vcsr::launch_panel_spmm(view(p), false, dB, ldb, dC, ldc, O,
-                                 (cudaStream_t)stream, launches);
+                                 (cudaStream_t)stream, launches, p->side, p->fork, p->join);
 }
 
 vcsr_status vcsr_spmm_host(vcsr_plan *p, const float *hB, float *hC, int O,

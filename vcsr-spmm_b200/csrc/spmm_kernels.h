@@ -14,8 +14,9 @@ struct PanelDevView {
   const int4 *units = nullptr;    // {vector, begin, end, split slot or -1}
   const int *row_ptr = nullptr;   // CSR mode only
   int n_units = 0;
-  const int *short_idx = nullptr; // units walked by one sub-warp each
-  int n_short = 0;
+  const int4 *batches = nullptr;  // {v0, v1, first union column, end}: consecutive
+  int n_batches = 0;              // short vectors walked by one sub-warp each
+  const int *vec_ptr = nullptr;   // union offsets of the vectors (num_vectors + 1)
   const int *long_idx = nullptr;  // units walked by a whole warp
   int n_long = 0;
   const int2 *parts = nullptr;    // per split slot: {split vector, part}
@@ -39,8 +40,12 @@ struct LaunchShape {
 
 LaunchShape pick_shape(int O, int R, bool vec4);
 
+// Launches the long-unit kernel (on `side`, forked from and joined back to
+// `st` with the two events, when there is short work too) and the short-work
+// kernel (on `st`).  side may be null: then both run on `st`.
 vcsr_status launch_panel_spmm(const PanelDevView &P, bool rowptr,
                               const float *B, int ldb, float *C, int ldc, int O,
-                              cudaStream_t st, int *launches);
+                              cudaStream_t st, int *launches, cudaStream_t side,
+                              cudaEvent_t fork, cudaEvent_t join);
 
 }  // namespace vcsr

@@ -275,14 +275,55 @@ __device__ __forceinline__ void load_group(const float *__restrict__ Bk, int ldb
   }
 }
 
-template <int R, int NV, int VW, int UN, bool FULL>
+// Vector boundaries inside a batch of consecutive vectors: `v` is the vector
+// being summed, `ve` the union index where it ends (svp holds vec_ptr[v0..v1]).
+struct BatchCursor {
+  int v, ve, v0;
+  const int *svp;
+};
+
+template <int R, int NV, int VW>
+__device__ __forceinline__ void store_rows(float *__restrict__ C, int ldc, int M, int row0,
+                                           const int (&kk)[NV], const bool (&ok)[NV],
+                                           const typename VecT<VW>::T (&out)[R][NV]) {
+  using V = VecT<VW>;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int row = row0 + r;
+    if (row < M) {
+#pragma unroll
+      for (int v = 0; v < NV; ++v)
+        if (ok[v]) V::stcs(C + (size_t)row * ldc + kk[v], out[r][v]);
+    }
+  }
+}
+
+// Write the finished vector(s) before union index `a` and start the next.
+template <int R, int NV, int VW>
+__device__ __forceinline__ void cross_boundaries(int a, BatchCursor &bc, Acc<R, NV, VW> &acc,
+                                                 float *__restrict__ C, int ldc, int M,
+                                                 const int (&kk)[NV], const bool (&ok)[NV]) {
+  while (a >= bc.ve) {
+    typename VecT<VW>::T o[R][NV];
+    acc.store(o);
+    store_rows<R, NV, VW>(C, ldc, M, bc.v * R, kk, ok, o);
+    acc.zero();
+    ++bc.v;
+    bc.ve = bc.svp[bc.v - bc.v0 + 1];
+  }
+}
+
+template <int R, int NV, int VW, int UN, bool FULL, bool BATCH>
 __device__ __forceinline__ void fma_group(const float *sval, int j0, int step, int n,
                                           const typename VecT<VW>::T (&b)[UN][NV],
-                                          Acc<R, NV, VW> &acc) {
+                                          Acc<R, NV, VW> &acc, int cbase, BatchCursor &bc,
+                                          float *__restrict__ C, int ldc, int M,
+                                          const int (&kk)[NV], const bool (&ok)[NV]) {
 #pragma unroll
   for (int q = 0; q < UN; ++q) {
     const int j = j0 + q * step;
     if (FULL || j < n) {
+      if constexpr (BATCH) cross_boundaries<R, NV, VW>(cbase + j, bc, acc, C, ldc, M, kk, ok);
       float a[R];
       load_vals_smem<R>(sval, j, a);
       acc.fma(a, b[q]);
@@ -290,16 +331,20 @@ __device__ __forceinline__ void fma_group(const float *sval, int j0, int step, i
   }
 }
 
-// One team walks one unit.  cg / ncg: this lane's column group and the number
-// of column groups (1 for a sub-warp team); t / T: lane index and size of the
-// team for staging; tmask: the team's lanes.  Leaves the column-group sums
-// reduced into the lanes of every column group.
-template <int R, int NV, int VW>
+// One team walks union columns [begin, end).  cg / ncg: this lane's column
+// group and the number of column groups (1 for a sub-warp team); t / T: lane
+// index and size of the team for staging; tmask: the team's lanes.
+// Without BATCH the columns belong to one vector and its column-group sums
+// are left reduced in `out`.  With BATCH (ncg = 1) they span vectors
+// [bc.v0, v1): each vector's rows are written to C when its last column has
+// been added, the last ones (and trailing empty vectors) at the end.
+template <int R, int NV, int VW, bool BATCH>
 __device__ __forceinline__ void walk_unit(
-    const PanelDevView &P, const float *__restrict__ B, int ldb, const int4 &U,
+    const PanelDevView &P, const float *__restrict__ B, int ldb, int begin, int end,
     const int (&kk)[NV], const bool (&ok)[NV], int cg, int ncg, int t, int T,
     unsigned tmask, int L, int chunk, int *buf_col, float *buf_val,
-    typename VecT<VW>::T (&out)[R][NV]) {
+    typename VecT<VW>::T (&out)[R][NV], BatchCursor &bc, int v1,
+    float *__restrict__ C, int ldc) {
   using V = VecT<VW>;
   using Tv = typename V::T;
   constexpr int UN = unroll_for<R, NV, VW>();
@@ -307,7 +352,6 @@ __device__ __forceinline__ void walk_unit(
   acc.zero();
   const float *Bk = B + kk[0];
   const int vstride = L * VW;
-  const int begin = U.y, end = U.z;
   if (begin < end) {
     // prologue: stage chunk 0 into buffer 0
     int n0 = min(chunk, end - begin);
@@ -337,7 +381,8 @@ __device__ __forceinline__ void walk_unit(
       for (int g = 0; g < nfull; g += 2) {
         if (g + 1 < nfull)
           load_group<NV, VW, UN, true>(Bk, ldb, scol, j + gstep, ncg, n, ok, vstride, b1);
-        fma_group<R, NV, VW, UN, true>(sval, j, ncg, n, b0, acc);
+        fma_group<R, NV, VW, UN, true, BATCH>(sval, j, ncg, n, b0, acc, c0, bc, C, ldc,
+                                              P.M, kk, ok);
         if (g + 1 >= nfull) {
           j += gstep;
           break;
@@ -345,16 +390,28 @@ __device__ __forceinline__ void walk_unit(
         if (g + 2 < nfull)
           load_group<NV, VW, UN, true>(Bk, ldb, scol, j + 2 * gstep, ncg, n, ok, vstride,
                                        b0);
-        fma_group<R, NV, VW, UN, true>(sval, j + gstep, ncg, n, b1, acc);
+        fma_group<R, NV, VW, UN, true, BATCH>(sval, j + gstep, ncg, n, b1, acc, c0, bc, C,
+                                              ldc, P.M, kk, ok);
         j += 2 * gstep;
       }
       if (j < n) {
         load_group<NV, VW, UN, false>(Bk, ldb, scol, j, ncg, n, ok, vstride, b0);
-        fma_group<R, NV, VW, UN, false>(sval, j, ncg, n, b0, acc);
+        fma_group<R, NV, VW, UN, false, BATCH>(sval, j, ncg, n, b0, acc, c0, bc, C, ldc,
+                                               P.M, kk, ok);
       }
       __syncwarp(tmask);  // everyone is done with `cur` before it is refilled
       cur ^= 1;
     }
+  }
+  if constexpr (BATCH) {
+    // the last vector and any empty vectors after it
+    while (bc.v < v1) {
+      acc.store(out);
+      store_rows<R, NV, VW>(C, ldc, P.M, bc.v * R, kk, ok, out);
+      acc.zero();
+      ++bc.v;
+    }
+    return;
   }
   acc.store(out);
   // sum the column groups: fixed xor tree over the lane bits above L
@@ -455,60 +512,42 @@ __device__ __forceinline__ void finish_unit(
   if ((threadIdx.x & 31) == lead_lane) *ctr = 0;  // ready for the next launch
 }
 
+constexpr int kBatchVecs = 64;  // vectors per batch at most
+constexpr int kBatchVP = 68;    // staged vec_ptr entries per team (>= kBatchVecs + 1)
+
+// Short work: one sub-warp per item.  Plans: a batch of consecutive short
+// vectors (for R <= 2 the sub-warp streams through all of them and writes
+// each vector's rows at its boundary; for R >= 4 a batch is one vector).
+// ROWPTR (plain CSR): one row.
 template <int R, int NV, int VW, bool ROWPTR>
 __global__ void __launch_bounds__(256, (min_blocks_for<R, NV, VW>()))
-    panel_spmm_kernel(const PanelDevView P, const float *__restrict__ B, int ldb,
-                      float *__restrict__ C, int ldc, int O, int lshift,
-                      int n_otiles, int W, int chunk) {
-  using V = VecT<VW>;
-  using Tv = typename V::T;
+    panel_short_kernel(const PanelDevView P, const float *__restrict__ B, int ldb,
+                       float *__restrict__ C, int ldc, int O, int lshift, int n_otiles,
+                       int W, int chunk) {
+  using Tv = typename VecT<VW>::T;
+  constexpr bool kBatch = !ROWPTR && R <= 2;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int L = 1 << lshift;
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  const int G = 32 >> lshift;  // sub-warps per warp
-  const int sub = lane >> lshift;
-  const int sl = lane & (L - 1);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int G = 32 >> lshift, sub = lane >> lshift, sl = lane & (L - 1);
   const unsigned submask = (L == 32) ? 0xffffffffu : (((1u << L) - 1u) << (sub * L));
-  // per warp: 2 buffers x (G*chunk) columns x (1 int + R floats)
-  const int wcols = G * chunk;
-  int *wcol = reinterpret_cast<int *>(smem_raw) + (size_t)warp * 2 * wcols * (R + 1);
-  float *wval = reinterpret_cast<float *>(wcol + 2 * wcols);
-  const int n_short = ROWPTR ? P.n_units : P.n_short;
-  const int n_long = ROWPTR ? 0 : P.n_long;
-  const int n_sg = (n_short + G - 1) / G;
-  const long long per_tile = (long long)n_long + n_sg;
+  // per warp: G teams x 2 buffers x chunk columns x (1 int + R floats), then
+  // G staged vec_ptr windows
+  int *wcol = reinterpret_cast<int *>(smem_raw) +
+              (size_t)warp * (2 * G * chunk * (R + 1) + G * kBatchVP);
+  float *wval = reinterpret_cast<float *>(wcol + 2 * G * chunk);
+  int *svp = reinterpret_cast<int *>(wval + (size_t)2 * G * chunk * R) + sub * kBatchVP;
+  int *bcol = wcol + sub * chunk * 2;
+  float *bval = wval + (size_t)sub * chunk * 2 * R;
+  const int n_sub = ROWPTR ? P.n_units : P.n_batches;
+  const long long per_tile = (n_sub + G - 1) / G;
   const long long n_items = per_tile * n_otiles;
   const long long nwarps = (long long)gridDim.x * (blockDim.x >> 5);
   for (long long item = (long long)blockIdx.x * (blockDim.x >> 5) + warp; item < n_items;
        item += nwarps) {
     const int ot = (int)(item / per_tile);
-    const long long w = item - (long long)ot * per_tile;
-    int4 U;
-    int cg, ncg, t, T, lead;
-    unsigned tmask;
-    int *bcol;
-    float *bval;
-    int chk;
-    if (w < n_long) {  // the whole warp on one long unit
-      U = __ldg(P.units + __ldg(P.long_idx + w));
-      cg = sub; ncg = G; t = lane; T = 32; tmask = 0xffffffffu; lead = 0;
-      bcol = wcol; bval = wval; chk = wcols;
-    } else {  // one short unit per sub-warp
-      const long long s = (w - n_long) * G + sub;
-      if (s >= n_short) {
-        U = make_int4(0, 0, 0, -2);  // idle sub-warp
-      } else if constexpr (ROWPTR) {
-        U = make_int4((int)s, __ldg(P.row_ptr + s), __ldg(P.row_ptr + s + 1), -1);
-      } else {
-        U = __ldg(P.units + __ldg(P.short_idx + s));
-      }
-      cg = 0; ncg = 1; t = sl; T = L; tmask = submask; lead = sub * L;
-      bcol = wcol + sub * chunk * 2;
-      bval = wval + (size_t)sub * chunk * 2 * R;
-      chk = chunk;
-    }
-    if (U.w == -2) continue;
+    const long long s = (item - (long long)ot * per_tile) * G + sub;
+    if (s >= n_sub) continue;  // idle sub-warp
     int kk[NV];
     bool ok[NV];
 #pragma unroll
@@ -517,38 +556,102 @@ __global__ void __launch_bounds__(256, (min_blocks_for<R, NV, VW>()))
       ok[v] = kk[v] < O;
     }
     Tv acc[R][NV];
-    walk_unit<R, NV, VW>(P, B, ldb, U, kk, ok, cg, ncg, t, T, tmask, L, chk, bcol,
-                         bval, acc);
-    finish_unit<R, NV, VW>(P, C, ldc, U, ot, kk, ok, cg, ncg, lead, tmask, acc);
+    BatchCursor bc{0, 0, 0, nullptr};
+    if constexpr (kBatch) {
+      const int4 bt = __ldg(P.batches + s);  // {v0, v1, first column, end column}
+      for (int i = sl; i <= bt.y - bt.x; i += L) svp[i] = __ldg(P.vec_ptr + bt.x + i);
+      __syncwarp(submask);
+      bc = BatchCursor{bt.x, svp[1], bt.x, svp};
+      walk_unit<R, NV, VW, true>(P, B, ldb, bt.z, bt.w, kk, ok, 0, 1, sl, L, submask, L,
+                                 chunk, bcol, bval, acc, bc, bt.y, C, ldc);
+      __syncwarp(submask);  // svp is rewritten by the next batch
+    } else {
+      int4 U;
+      if constexpr (ROWPTR) {
+        U = make_int4((int)s, __ldg(P.row_ptr + s), __ldg(P.row_ptr + s + 1), -1);
+      } else {
+        const int4 bt = __ldg(P.batches + s);  // one vector
+        U = make_int4(bt.x, bt.z, bt.w, -1);
+      }
+      walk_unit<R, NV, VW, false>(P, B, ldb, U.y, U.z, kk, ok, 0, 1, sl, L, submask, L,
+                                  chunk, bcol, bval, acc, bc, 0, C, ldc);
+      store_rows<R, NV, VW>(C, ldc, P.M, U.x * R, kk, ok, acc);
+    }
+  }
+}
+
+// Long work: a whole warp per long unit or split part, its sub-warps taking
+// every G-th union column; split parts finish through the part tickets.
+template <int R, int NV, int VW>
+__global__ void __launch_bounds__(256, (min_blocks_for<R, NV, VW>() < 2
+                                            ? min_blocks_for<R, NV, VW>()
+                                            : 2))
+    panel_long_kernel(const PanelDevView P, const float *__restrict__ B, int ldb,
+                      float *__restrict__ C, int ldc, int O, int lshift, int n_otiles,
+                      int W, int chunk) {
+  using Tv = typename VecT<VW>::T;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int L = 1 << lshift;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int G = 32 >> lshift, sub = lane >> lshift, sl = lane & (L - 1);
+  const int wcols = G * chunk;
+  int *wcol = reinterpret_cast<int *>(smem_raw) +
+              (size_t)warp * (2 * wcols * (R + 1) + G * kBatchVP);
+  float *wval = reinterpret_cast<float *>(wcol + 2 * wcols);
+  const long long per_tile = P.n_long;
+  const long long n_items = per_tile * n_otiles;
+  const long long nwarps = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long item = (long long)blockIdx.x * (blockDim.x >> 5) + warp; item < n_items;
+       item += nwarps) {
+    const int ot = (int)(item / per_tile);
+    const long long w = item - (long long)ot * per_tile;
+    int kk[NV];
+    bool ok[NV];
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      kk[v] = ot * W + v * (L * VW) + sl * VW;
+      ok[v] = kk[v] < O;
+    }
+    Tv acc[R][NV];
+    BatchCursor bc{0, 0, 0, nullptr};
+    const int4 U = __ldg(P.units + __ldg(P.long_idx + w));
+    walk_unit<R, NV, VW, false>(P, B, ldb, U.y, U.z, kk, ok, sub, G, lane, 32, 0xffffffffu,
+                                L, wcols, wcol, wval, acc, bc, 0, C, ldc);
+    finish_unit<R, NV, VW>(P, C, ldc, U, ot, kk, ok, sub, G, 0, 0xffffffffu, acc);
   }
 }
 
 using KernelFn = void (*)(const PanelDevView, const float *, int, float *, int, int,
                           int, int, int, int);
 
-template <int R, int NV, int VW, bool ROWPTR>
-constexpr KernelFn kfn() {
-  return panel_spmm_kernel<R, NV, VW, ROWPTR>;
+template <int R, int NV, int VW>
+KernelFn pick_rv(bool is_long, bool rowptr) {
+  if (is_long) return panel_long_kernel<R, NV, VW>;
+  if constexpr (R == 1) {
+    if (rowptr) return panel_short_kernel<1, NV, VW, true>;
+  }
+  return panel_short_kernel<R, NV, VW, false>;
 }
 
-KernelFn select_kernel(int R, int NV, int VW, bool rowptr) {
-  if (rowptr) {
-    if (NV == 1) return VW == 4 ? kfn<1, 1, 4, true>() : kfn<1, 1, 1, true>();
-    return VW == 4 ? kfn<1, 2, 4, true>() : kfn<1, 2, 1, true>();
+template <int R>
+KernelFn pick_r(int NV, int VW, bool is_long, bool rowptr) {
+  if constexpr (R == 16) {
+    return VW == 4 ? pick_rv<16, 1, 4>(is_long, rowptr) : pick_rv<16, 1, 1>(is_long, rowptr);
+  } else {
+    if (NV == 1)
+      return VW == 4 ? pick_rv<R, 1, 4>(is_long, rowptr) : pick_rv<R, 1, 1>(is_long, rowptr);
+    return VW == 4 ? pick_rv<R, 2, 4>(is_long, rowptr) : pick_rv<R, 2, 1>(is_long, rowptr);
   }
-#define VCSR_SEL(RR)                                                              \
-  case RR:                                                                        \
-    if (NV == 1) return VW == 4 ? kfn<RR, 1, 4, false>() : kfn<RR, 1, 1, false>(); \
-    return VW == 4 ? kfn<RR, 2, 4, false>() : kfn<RR, 2, 1, false>();
+}
+
+KernelFn select_kernel(int R, int NV, int VW, bool is_long, bool rowptr) {
   switch (R) {
-    VCSR_SEL(1)
-    VCSR_SEL(2)
-    VCSR_SEL(4)
-    VCSR_SEL(8)
-    case 16:
-      return VW == 4 ? kfn<16, 1, 4, false>() : kfn<16, 1, 1, false>();
+    case 1: return pick_r<1>(NV, VW, is_long, rowptr);
+    case 2: return pick_r<2>(NV, VW, is_long, rowptr);
+    case 4: return pick_r<4>(NV, VW, is_long, rowptr);
+    case 8: return pick_r<8>(NV, VW, is_long, rowptr);
+    case 16: return pick_r<16>(NV, VW, is_long, rowptr);
   }
-#undef VCSR_SEL
   return nullptr;
 }
 
@@ -594,39 +697,70 @@ int stage_chunk_cols(int R, int G) {
   return c & ~3;
 }
 
-vcsr_status launch_panel_spmm(const PanelDevView &P, bool rowptr, const float *B,
-                              int ldb, float *C, int ldc, int O, cudaStream_t st,
-                              int *launches) {
-  if (launches) *launches = 0;
-  if (O <= 0 || P.n_units <= 0) return VCSR_OK;
-  const bool vec4 = (O % 4 == 0) && (ldb % 4 == 0) && (ldc % 4 == 0) &&
-                    ((uintptr_t)B % 16 == 0) && ((uintptr_t)C % 16 == 0);
-  const LaunchShape s = pick_shape(O, P.R, vec4);
-  KernelFn fn = select_kernel(P.R, s.NV, s.VW, rowptr);
-  if (!fn) return fail(VCSR_ERR_UNSUPPORTED, "no kernel for R=%d", P.R);
-  if (!rowptr && P.n_split_units > 0 && (O > P.pstride || s.n_otiles > P.counter_stride))
-    return fail(VCSR_ERR_INVALID, "O=%d exceeds the plan's max_O=%d", O, P.pstride);
+namespace {
+
+vcsr_status launch_one(KernelFn fn, const PanelDevView &P, long long team_items, int G,
+                       const LaunchShape &s, int chunk, size_t smem, const float *B, int ldb,
+                       float *C, int ldc, int O, cudaStream_t st) {
   const int threads = 256;
-  const int G = 32 >> s.lshift;
-  const int chunk = stage_chunk_cols(P.R, G);
-  const size_t smem = (size_t)(threads / 32) * 2 * G * chunk * (P.R + 1) * 4;
   if (smem > 48 * 1024)
     VCSR_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    (int)smem));
   int per_sm = 0;
   VCSR_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem));
   if (per_sm <= 0) per_sm = 1;
-  const int n_short = rowptr ? P.n_units : P.n_short;
-  const int n_long = rowptr ? 0 : P.n_long;
-  const long long items = ((long long)n_long + (n_short + G - 1) / G) * s.n_otiles;
+  const long long items = team_items * s.n_otiles;
   long long blocks = (items + (threads / 32) - 1) / (threads / 32);
   const long long cap = (long long)sm_count() * per_sm;
-  if (blocks > cap) blocks = cap;
-  if (blocks < 1) blocks = 1;
+  blocks = blocks > cap ? cap : (blocks < 1 ? 1 : blocks);
   fn<<<(int)blocks, threads, smem, st>>>(P, B, ldb, C, ldc, O, s.lshift, s.n_otiles, s.W,
                                          chunk);
   VCSR_CUDA(cudaGetLastError());
-  if (launches) *launches = 1;
+  return VCSR_OK;
+}
+
+}  // namespace
+
+vcsr_status launch_panel_spmm(const PanelDevView &P, bool rowptr, const float *B, int ldb,
+                              float *C, int ldc, int O, cudaStream_t st, int *launches,
+                              cudaStream_t side, cudaEvent_t fork, cudaEvent_t join) {
+  if (launches) *launches = 0;
+  const int n_short = rowptr ? P.n_units : P.n_batches;
+  const int n_long = rowptr ? 0 : P.n_long;
+  if (O <= 0 || n_short + n_long <= 0) return VCSR_OK;
+  const bool vec4 = (O % 4 == 0) && (ldb % 4 == 0) && (ldc % 4 == 0) &&
+                    ((uintptr_t)B % 16 == 0) && ((uintptr_t)C % 16 == 0);
+  const LaunchShape s = pick_shape(O, P.R, vec4);
+  if (!rowptr && P.n_split_units > 0 && (O > P.pstride || s.n_otiles > P.counter_stride))
+    return fail(VCSR_ERR_INVALID, "O=%d exceeds the plan's max_O=%d", O, P.pstride);
+  const int G = 32 >> s.lshift;
+  const int chunk = stage_chunk_cols(P.R, G);
+  const size_t smem = (size_t)8 * (2 * G * chunk * (P.R + 1) + G * kBatchVP) * 4;
+  const bool both = n_short > 0 && n_long > 0 && side != nullptr;
+  if (both) {  // the long units run beside the short ones on the plan's side stream
+    VCSR_CUDA(cudaEventRecord(fork, st));
+    VCSR_CUDA(cudaStreamWaitEvent(side, fork, 0));
+  }
+  int n = 0;
+  if (n_long > 0) {
+    KernelFn fl = select_kernel(P.R, s.NV, s.VW, true, false);
+    if (!fl) return fail(VCSR_ERR_UNSUPPORTED, "no kernel for R=%d", P.R);
+    VCSR_TRY(launch_one(fl, P, n_long, G, s, chunk, smem, B, ldb, C, ldc, O,
+                        both ? side : st));
+    ++n;
+  }
+  if (n_short > 0) {
+    KernelFn fs = select_kernel(P.R, s.NV, s.VW, false, rowptr);
+    if (!fs) return fail(VCSR_ERR_UNSUPPORTED, "no kernel for R=%d", P.R);
+    VCSR_TRY(launch_one(fs, P, (n_short + G - 1) / G, G, s, chunk, smem, B, ldb, C, ldc, O,
+                        st));
+    ++n;
+  }
+  if (both) {
+    VCSR_CUDA(cudaEventRecord(join, side));
+    VCSR_CUDA(cudaStreamWaitEvent(st, join, 0));
+  }
+  if (launches) *launches = n;
   return VCSR_OK;
 }
 
@@ -646,7 +780,8 @@ extern "C" vcsr_status vcsr_csr_spmm(int M, const int *d_row_ptr, const int *d_c
   P.n_units = M;
   P.M = M;
   P.R = 1;
-  return vcsr::launch_panel_spmm(P, true, dB, O, dC, O, O, (cudaStream_t)stream, nullptr);
+  return vcsr::launch_panel_spmm(P, true, dB, O, dC, O, O, (cudaStream_t)stream, nullptr,
+                                 nullptr, nullptr, nullptr);
 }
 
 // ------------------------------------------------- allocation-free CSR SpMM
@@ -792,7 +927,9 @@ __global__ void __launch_bounds__(256, (min_blocks_for<1, NV, VW>()))
       ok[v] = kk[v] < O;
     }
     Tv acc[1][NV];
-    walk_unit<1, NV, VW>(P, B, ldb, U, kk, ok, cg, ncg, t, T, tmask, L, chk, bcol, bval, acc);
+    BatchCursor bc{0, 0, 0, nullptr};
+    walk_unit<1, NV, VW, false>(P, B, ldb, U.y, U.z, kk, ok, cg, ncg, t, T, tmask, L, chk,
+                                bcol, bval, acc, bc, 0, C, ldc);
     finish_unit<1, NV, VW>(P, C, ldc, U, ot, kk, ok, cg, ncg, lead, tmask, acc);
   }
 }
