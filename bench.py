@@ -271,6 +271,8 @@ def run_ours(args):
         V.gen_dense_device(dB, args.seed + 1000, lo, 1.0)
     if world > 1:
         torch.cuda.synchronize()
+        D.broadcast_b(dist, dB, 0)  # first collective on this buffer: NCCL set-up
+        torch.cuda.synchronize()
         dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)

@@ -189,6 +189,14 @@ vcsr_status vcsr_mgpu_set_b(vcsr_mgpu *m, const float *hB, int O, float *bcast_m
   VCSR_CUDA(cudaMemcpyAsync(m->dB[0], hB, sizeof(float) * nb, cudaMemcpyHostToDevice,
                             m->streams[0]));
   VCSR_CUDA(cudaStreamSynchronize(m->streams[0]));
+  // the first broadcast on a buffer carries NCCL's set-up; run it untimed
+  m->nccl.GroupStart();
+  for (int i = 0; i < m->n; ++i) {
+    cudaSetDevice(m->devs[i]);
+    m->nccl.Broadcast(m->dB[i], m->dB[i], nb, ncclFloat, 0, m->comms[i], m->streams[i]);
+  }
+  if (m->nccl.GroupEnd() != ncclSuccess) return fail(VCSR_ERR_NCCL, "ncclGroupEnd failed");
+  VCSR_TRY(wait_all(m, true));
   for (int i = 0; i < m->n; ++i) {
     cudaSetDevice(m->devs[i]);
     VCSR_CUDA(cudaEventRecord(m->ev0[i], m->streams[i]));
