@@ -151,6 +151,13 @@ vcsr_status vcsr_vcsr_to_host(const vcsr_vcsr *dev, vcsr_vcsr *host);
 typedef struct vcsr_plan vcsr_plan;
 
 #define VCSR_PLAN_REFERENCE_FORMAT 1 /* also keep the segment-major VCSR */
+/* Run dense 16x16 blocks of A (>= panel_min_nnz entries) on the tensor cores
+ * in TF32 (tcgen05.mma kind::tf32, FP32 accumulation): the reference's
+ * tensor-core variant (src/vcsr_tc.cu:122-195, FP16 WMMA) on B200.  Results
+ * then match the FP32 CSR sum to about 1e-3 relative L2 instead of 1e-5.
+ * Needs O and ldb multiples of 4 and a 16-byte aligned B at call time
+ * (VCSR_ERR_UNSUPPORTED otherwise). */
+#define VCSR_PLAN_TF32_PANELS 2
 
 typedef struct vcsr_plan_params {
   int segw;     /* column segment width (--segw) */
@@ -161,6 +168,8 @@ typedef struct vcsr_plan_params {
                    else 1, 2, 4, 8 or 16 */
   int chunk;    /* max union columns per work unit; 0 = choose */
   int flags;    /* VCSR_PLAN_* */
+  int panel_min_nnz; /* entries that make a 16x16 block a TF32 panel
+                        (1..256; 0 = 128) */
 } vcsr_plan_params;
 
 typedef struct vcsr_plan_info {
@@ -175,6 +184,9 @@ typedef struct vcsr_plan_info {
   int64_t panel_bytes; /* device bytes of the panel layout */
   int has_reference_format;
   double build_ms;    /* wall time of vcsr_plan_create */
+  int num_panel_blocks;     /* dense 16x16 blocks on the TF32 path */
+  int num_panel_row_blocks; /* row blocks holding them */
+  int64_t panel_nnz;        /* entries of A inside those blocks */
 } vcsr_plan_info;
 
 void vcsr_plan_params_default(vcsr_plan_params *p);
@@ -207,6 +219,14 @@ vcsr_status vcsr_spmm(const vcsr_plan *plan, const float *dB, int ldb,
  * stream.  Host buffers should be pinned for full PCIe speed. */
 vcsr_status vcsr_spmm_host(vcsr_plan *plan, const float *hB, float *hC, int O,
                            vcsr_stream_t stream);
+
+/* Synchronises `stream` and reports a failure that the plan's kernels
+ * recorded on the device since the last check (the tensor-core panel kernel
+ * bounds every wait on its pipeline barriers and records the first one that
+ * ran out): VCSR_ERR_TIMEOUT with the barrier named in vcsr_last_error(); the
+ * record is cleared.  vcsr_spmm_host checks on its own.  No counterpart in
+ * the reference (its kernels have no waits). */
+vcsr_status vcsr_plan_check(vcsr_plan *plan, vcsr_stream_t stream);
 
 /* ------------------------------------------------------------ peer paths */
 

@@ -14,7 +14,9 @@
 
 #include "common.h"
 #include "panel.h"
+#include "panel_tc.h"
 #include "spmm_kernels.h"
+#include "spmm_tc.h"
 
 using vcsr::fail;
 
@@ -43,6 +45,11 @@ struct vcsr_plan {
   // optional segment-major VCSR (include/vcsr.hpp:12-23 layout)
   bool has_ref = false;
   vcsr_vcsr ref{};
+  // dense 16x16 panels on the tcgen05 TF32 path (VCSR_PLAN_TF32_PANELS)
+  int *d_rb_row = nullptr, *d_rb_ptr = nullptr, *d_blk_col = nullptr, *d_err = nullptr;
+  float *d_blk_val = nullptr;
+  int n_panel_rb = 0, n_panel_blocks = 0;
+  int64_t panel_nnz = 0;
   // side stream and events for running long units beside short ones
   cudaStream_t side = nullptr;
   cudaEvent_t fork = nullptr, join = nullptr;
@@ -72,6 +79,8 @@ void release(vcsr_plan *p) {
   cudaFree(p->d_parts); cudaFree(p->d_svecs); cudaFree(p->d_partials);
   cudaFree(p->d_counters); cudaFree(p->d_stage_B); cudaFree(p->d_stage_C);
   if (p->has_ref) vcsr_vcsr_free(&p->ref, VCSR_DEVICE);
+  cudaFree(p->d_rb_row); cudaFree(p->d_rb_ptr); cudaFree(p->d_blk_col);
+  cudaFree(p->d_blk_val); cudaFree(p->d_err);
   if (p->side) cudaStreamDestroy(p->side);
   if (p->fork) cudaEventDestroy(p->fork);
   if (p->join) cudaEventDestroy(p->join);
@@ -188,6 +197,7 @@ void vcsr_plan_params_default(vcsr_plan_params *p) {
   p->vec_rows = 0;
   p->chunk = 0;
   p->flags = 0;
+  p->panel_min_nnz = 0;
 }
 
 vcsr_status vcsr_plan_create(const vcsr_csr *csr, int csr_where,
@@ -229,10 +239,37 @@ vcsr_status vcsr_plan_create(const vcsr_csr *csr, int csr_where,
     if (s != VCSR_OK) { delete p; return s; }
   }
 
+  // TF32 panels: the dense 16x16 blocks go to the tensor-core path, the
+  // rest (the residual) to the row-stationary layout below
+  vcsr::TcHost tc;
+  std::vector<int> r_rp, r_col;
+  std::vector<float> r_val;
+  vcsr_csr work = h;
+  if ((params->flags & VCSR_PLAN_TF32_PANELS) && h.M > 0) {
+    if (params->panel_min_nnz < 0 || params->panel_min_nnz > 256) {
+      if (owned) vcsr_csr_free(&h, VCSR_HOST);
+      delete p;
+      return fail(VCSR_ERR_INVALID, "panel_min_nnz must be in [0, 256]");
+    }
+    const int min_nnz = params->panel_min_nnz > 0 ? params->panel_min_nnz : 128;
+    vcsr_status s0 = vcsr::split_dense_panels(h, min_nnz, &tc, r_rp, r_col, r_val);
+    if (s0 != VCSR_OK) {
+      if (owned) vcsr_csr_free(&h, VCSR_HOST);
+      delete p;
+      return s0;
+    }
+    work.nnz = r_rp.back();
+    work.row_ptr = r_rp.data();
+    work.col = r_col.data();
+    work.val = r_val.data();
+    p->n_panel_rb = (int)tc.rb_row.size();
+    p->n_panel_blocks = (int)tc.blk_col.size();
+    p->panel_nnz = (int64_t)h.nnz - work.nnz;
+  }
   vcsr::PanelHost ph;
   int R = params->vec_rows;
-  if (R == 0) R = vcsr::choose_vec_rows(h, nullptr);
-  vcsr_status s = vcsr::build_panel_host(h, R, params->chunk, sms, &ph);
+  if (R == 0) R = vcsr::choose_vec_rows(work, nullptr);
+  vcsr_status s = vcsr::build_panel_host(work, R, params->chunk, sms, &ph);
   if (s != VCSR_OK) {
     if (owned) vcsr_csr_free(&h, VCSR_HOST);
     delete p;
@@ -307,6 +344,19 @@ vcsr_status vcsr_plan_create(const vcsr_csr *csr, int csr_where,
     delete p;
     return s;
   }
+  if (p->n_panel_rb > 0) {
+    std::vector<int> zero1(1, 0);
+    if ((s = upload(&p->d_rb_row, tc.rb_row, st, &p->panel_bytes)) ||
+        (s = upload(&p->d_rb_ptr, tc.rb_ptr, st, &p->panel_bytes)) ||
+        (s = upload(&p->d_blk_col, tc.blk_col, st, &p->panel_bytes)) ||
+        (s = upload(&p->d_blk_val, tc.blk_val, st, &p->panel_bytes)) ||
+        (s = upload(&p->d_err, zero1, st, &p->panel_bytes))) {
+      if (owned) vcsr_csr_free(&h, VCSR_HOST);
+      release(p);
+      delete p;
+      return s;
+    }
+  }
   if (p->n_long > 0 && p->n_batches > 0) {
     cudaError_t e = cudaStreamCreateWithFlags(&p->side, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->fork, cudaEventDisableTiming);
@@ -375,6 +425,9 @@ vcsr_status vcsr_plan_get_info(const vcsr_plan *p, vcsr_plan_info *info) {
   info->panel_bytes = p->panel_bytes;
   info->has_reference_format = p->has_ref ? 1 : 0;
   info->build_ms = p->build_ms;
+  info->num_panel_blocks = p->n_panel_blocks;
+  info->num_panel_row_blocks = p->n_panel_rb;
+  info->panel_nnz = p->panel_nnz;
   return VCSR_OK;
 }
 
@@ -407,8 +460,22 @@ vcsr_status vcsr_spmm(const vcsr_plan *p, const float *dB, int ldb, float *dC,
     return fail(VCSR_ERR_INVALID,
                 "O=%d exceeds the plan's max_O=%d (split rows need scratch)", O,
                 p->pstride);
-  return vcsr::launch_panel_spmm(view(p), false, dB, ldb, dC, ldc, O,
-                                 (cudaStream_t)stream, launches, p->side, p->fork, p->join);
+  int n1 = 0, n2 = 0;
+  VCSR_TRY(vcsr::launch_panel_spmm(view(p), false, dB, ldb, dC, ldc, O, (cudaStream_t)stream,
+                                   &n1, p->side, p->fork, p->join));
+  if (p->n_panel_rb > 0) {  // C += dense panels * B on the tensor cores
+    vcsr::TcView tv;
+    tv.n_rb = p->n_panel_rb;
+    tv.rb_row = p->d_rb_row;
+    tv.rb_ptr = p->d_rb_ptr;
+    tv.blk_col = p->d_blk_col;
+    tv.blk_val = p->d_blk_val;
+    tv.M = p->M;
+    tv.err = p->d_err;
+    VCSR_TRY(vcsr::launch_tc_panels(tv, dB, p->N, ldb, dC, ldc, O, (cudaStream_t)stream, &n2));
+  }
+  if (launches) *launches = n1 + n2;
+  return VCSR_OK;
 }
 
 vcsr_status vcsr_spmm_host(vcsr_plan *p, const float *hB, float *hC, int O,
@@ -438,7 +505,24 @@ vcsr_status vcsr_spmm_host(vcsr_plan *p, const float *hB, float *hC, int O,
   VCSR_TRY(vcsr_spmm(p, p->d_stage_B, O, p->d_stage_C, O, O, stream, nullptr));
   if (nc) VCSR_CUDA(cudaMemcpyAsync(hC, p->d_stage_C, nc, cudaMemcpyDeviceToHost, st));
   VCSR_CUDA(cudaStreamSynchronize(st));
-  return VCSR_OK;
+  return p->d_err ? vcsr_plan_check(p, stream) : VCSR_OK;
+}
+
+vcsr_status vcsr_plan_check(vcsr_plan *p, vcsr_stream_t stream) {
+  vcsr::clear_error();
+  if (!p) return fail(VCSR_ERR_INVALID, "null plan");
+  cudaStream_t st = (cudaStream_t)stream;
+  VCSR_CUDA(cudaStreamSynchronize(st));
+  if (!p->d_err) return VCSR_OK;
+  int word = 0;
+  VCSR_CUDA(cudaMemcpyAsync(&word, p->d_err, sizeof(int), cudaMemcpyDeviceToHost, st));
+  VCSR_CUDA(cudaStreamSynchronize(st));
+  if (!word) return VCSR_OK;
+  VCSR_CUDA(cudaMemsetAsync(p->d_err, 0, sizeof(int), st));
+  VCSR_CUDA(cudaStreamSynchronize(st));
+  char msg[160];
+  vcsr::describe_tc_error(word, msg, sizeof msg);
+  return fail(VCSR_ERR_TIMEOUT, "%s", msg);
 }
 
 }  // extern "C"

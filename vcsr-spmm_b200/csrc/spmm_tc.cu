@@ -1,0 +1,374 @@
+// spmm_tc.cu — tcgen05 TF32 SpMM on dense 16x16 panels of A (sm_100a).
+//
+// A plan built with VCSR_PLAN_TF32_PANELS keeps every 16x16 block of A (rows
+// 16i.., columns 16j..) holding at least `panel_min_nnz` entries as a dense
+// TF32 tile; the other entries stay in the FP32 row-stationary layout and
+// are computed first (C written).  This kernel then adds the panels' product:
+// for one row block i and one 128-column slice of O,
+//     D[128 x 16] = sum over the row block's dense blocks j of
+//                   B[16j .. 16j+15, slice]^T (128 x 16)  x  A_ij^T (16 x 16)
+// in tensor memory, i.e. tcgen05.mma kind::tf32 with M = 128 (the O slice),
+// N = 16 (the block's rows), K = 16 (two K = 8 instructions).  Operand A is B
+// as stored (row-major, O contiguous): MN-major, loaded by 2-D TMA boxes of
+// 16 rows x 32 floats.  An MN-major TF32 operand has one shared-memory
+// layout, the 128-byte swizzle with 32-byte atoms (descriptor layout 1, TMA
+// CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B): the four 32-byte chunks of each
+// 128-byte row are exchanged by row % 4, so a swizzle atom is 4 rows (512
+// bytes) of K; with the plain 128-byte swizzle the MMA reads TF32 operands as
+// zeros.  Operand B is the dense block, pre-packed by the plan in the K-major
+// core-matrix order (8 rows x 16 bytes per core matrix, no swizzle) and
+// fetched with one 1-KB bulk copy.  This is the reference's tensor-core idea
+// (src/vcsr_tc.cu:122-195: one FP16 WMMA per depth step, 16x16 groups,
+// atomics into C) rebuilt with TF32 inputs, FP32 accumulation in TMEM, no
+// atomics, and the O dimension on the tensor core's M side.
+//
+// Roles (160 threads): warps 0-3 read the accumulator (warp w owns TMEM lanes
+// 32w..32w+31) and add it into C; warp 4 allocates TMEM and its lane 0 issues
+// the TMA loads (an S-stage ring, `full`/`empty` mbarriers) and the MMAs.
+// Two accumulators alternate between items so the epilogue of item t runs
+// while the MMAs of item t+1 are issued.  Every mbarrier wait is bounded:
+// after ~2^22 polls the kernel records which wait gave up, stops and frees
+// its TMEM.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <mutex>
+
+#include "common.h"
+#include "spmm_tc.h"
+
+namespace vcsr {
+namespace {
+
+constexpr int kStages = 4;
+constexpr int kBTileBytes = 16 * 128 * 4;  // 16 rows x 128 floats, 4 swizzled boxes
+constexpr int kABlockBytes = 16 * 16 * 4;  // one dense block
+constexpr int kStageBytes = kBTileBytes + kABlockBytes;
+constexpr int kThreads = 160;
+constexpr uint32_t kTmemCols = 32;  // two 16-column accumulators
+constexpr long long kPollLimit = 1ll << 22;
+
+// Where a bounded wait gave up (recorded in the plan's error word).
+enum WaitSite : int { kWaitFull = 1, kWaitEmpty = 2, kWaitAccFull = 3, kWaitAccFree = 4 };
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Bounded wait for the phase with the given parity; false when the poll
+// limit ran out (the site is recorded) or another thread already reported a
+// failure.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
+                                          volatile int *abort_flag, int site) {
+  const uint32_t a = smem_u32(bar);
+  for (long long i = 0; i < kPollLimit; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; "
+        "selp.u32 %0, 1, 0, p; }"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if ((i & 1023) == 1023 && *abort_flag) return false;
+  }
+  *abort_flag = site;
+  return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *tm, int x, int y,
+                                            uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(tm), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes,
+                                          uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Shared-memory matrix descriptor: start, leading and stride byte offsets
+// (16-byte units), version 1, layout type (0 = no swizzle, 1 = 128-byte
+// swizzle with 32-byte atoms).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo,
+                                              uint32_t layout) {
+  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46) | ((uint64_t)layout << 61);
+}
+
+// kind::tf32, D f32, A MN-major (bit 15), B K-major, N = 16, M = 128.
+constexpr uint32_t kInstrDesc = (1u << 4) | (2u << 7) | (2u << 10) | (1u << 15) |
+                                ((16u >> 3) << 17) | ((128u >> 4) << 24);
+
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %4, 0; "
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8}, p; }" ::"r"(
+          d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(kInstrDesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u),
+      "r"(0u)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+struct ItemCursor {  // walks (item, block) pairs of this CTA in order
+  int item, blk, nblk, rbi, oc;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_panel_kernel(const TcView V, const __grid_constant__ CUtensorMap tmB) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  // 1024-byte aligned stage ring (each K = 8 step starts on a 1-KB boundary)
+  unsigned char *base = reinterpret_cast<unsigned char *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  unsigned char *stage = base;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(base + kStages * kStageBytes);
+  uint64_t *full = bars, *empty = bars + kStages;
+  uint64_t *dfull = bars + 2 * kStages;      // accumulator b ready (count 1)
+  uint64_t *dfree = bars + 2 * kStages + 2;  // accumulator b read (count 128)
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 2 * kStages + 4);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(dfull + b, 1);
+      mbar_init(dfree + b, 128);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 4) {  // one warp allocates the accumulators
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_holder)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_holder;
+  const int n_items = V.n_rb * V.n_ochunks;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      // ---------------------------------------------- producer + MMA issue
+      auto item_of = [&](int t, ItemCursor &c) {
+        c.item = t;
+        c.blk = 0;
+        c.oc = t / V.n_rb;
+        c.rbi = t - c.oc * V.n_rb;
+        c.nblk = V.rb_ptr[c.rbi + 1] - V.rb_ptr[c.rbi];
+      };
+      ItemCursor ld;  // next (item, block) to load
+      item_of(blockIdx.x, ld);
+      long long g_load = 0, g_mma = 0;  // stages loaded / consumed so far
+      auto issue_load = [&]() -> bool {  // loads the next stage, false at the end
+        while (ld.item < n_items && ld.blk >= ld.nblk) item_of(ld.item + gridDim.x, ld);
+        if (ld.item >= n_items) return false;
+        const int s = (int)(g_load % kStages);
+        if (g_load >= kStages &&
+            !mbar_wait(empty + s, (uint32_t)(((g_load / kStages) - 1) & 1), abort_flag,
+                       kWaitEmpty))
+          return false;
+        unsigned char *st = stage + s * kStageBytes;
+        const int bi = V.rb_ptr[ld.rbi] + ld.blk;
+        const int j = V.blk_col[bi];
+        mbar_expect_tx(full + s, kStageBytes);
+        bulk_load(st + kBTileBytes, V.blk_val + (size_t)bi * 256, kABlockBytes, full + s);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          tma_load_2d(st + q * 2048, &tmB, ld.oc * 128 + 32 * q, 16 * j, full + s);
+        ++ld.blk;
+        ++g_load;
+        return true;
+      };
+      for (int s = 0; s < kStages - 1; ++s)
+        if (!issue_load()) break;
+      int lt = 0;  // local item count
+      for (int t = blockIdx.x; t < n_items && !*abort_flag; t += gridDim.x, ++lt) {
+        const int oc = t / V.n_rb, rbi = t - oc * V.n_rb;
+        const int nblk = V.rb_ptr[rbi + 1] - V.rb_ptr[rbi];
+        const int buf = lt & 1;
+        if (lt >= 2 && !mbar_wait(dfree + buf, (uint32_t)(((lt - 2) >> 1) & 1), abort_flag,
+                                  kWaitAccFree))
+          break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t dt = tmem + (uint32_t)(buf * 16);
+        for (int b = 0; b < nblk; ++b) {
+          const int s = (int)(g_mma % kStages);
+          if (!mbar_wait(full + s, (uint32_t)((g_mma / kStages) & 1), abort_flag, kWaitFull))
+            break;
+          unsigned char *st = stage + s * kStageBytes;
+          const uint32_t a_addr = smem_u32(st), b_addr = smem_u32(st + kBTileBytes);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            // A: MN atoms (32 floats) 2048 bytes apart (one TMA box each),
+            // K atoms (4 rows) 512 bytes apart; this K = 8 step starts at row 8h
+            const uint64_t ad = smem_desc(a_addr + h * 1024, 2048, 512, 1);
+            // B: core matrices 128 bytes apart along N, 256 along K
+            const uint64_t bd = smem_desc(b_addr + h * 512, 256, 128, 0);
+            mma_tf32(dt, ad, bd, (b > 0 || h > 0) ? 1u : 0u);
+          }
+          mma_commit(empty + s);
+          ++g_mma;
+          issue_load();  // refill: waits for the MMA of an older stage
+        }
+        mma_commit(dfull + buf);  // the plan lists only row blocks with dense blocks
+      }
+    }
+  } else {
+    // -------------------------------------------------------- epilogue
+    int lt = 0;
+    for (int t = blockIdx.x; t < n_items; t += gridDim.x, ++lt) {
+      const int oc = t / V.n_rb, rbi = t - oc * V.n_rb;
+      const int buf = lt & 1;
+      if (!mbar_wait(dfull + buf, (uint32_t)((lt >> 1) & 1), abort_flag, kWaitAccFull)) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      uint32_t r[16];
+      const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(buf * 16);
+      asm volatile(
+          "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+          "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+          : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+            "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]),
+            "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+          : "r"(taddr));
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      mbar_arrive(dfree + buf);
+      const int m = oc * 128 + warp * 32 + lane;  // column of C
+      const int row0 = V.rb_row[rbi];
+      if (m < V.O) {
+#pragma unroll
+        for (int n = 0; n < 16; ++n) {
+          const int row = row0 + n;
+          if (row < V.M) {
+            float *c = V.C + (size_t)row * V.ldc + m;
+            *c += __uint_as_float(r[n]);
+          }
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (threadIdx.x == 0 && *abort_flag) atomicCAS(V.err, 0, *abort_flag | (int)(blockIdx.x << 4));
+  if (warp == 4) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols));
+  }
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                   CUtensorMapFloatOOBfill);
+
+vcsr_status encode_fn(EncodeTiledFn *out) {
+  static EncodeTiledFn fn = nullptr;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lk(mu);
+  if (!fn) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    VCSR_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    if (q != cudaDriverEntryPointSuccess || !p)
+      return fail(VCSR_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled not available");
+    fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  *out = fn;
+  return VCSR_OK;
+}
+
+}  // namespace
+
+size_t tc_smem_bytes() { return (size_t)kStages * kStageBytes + 1024 + 256; }
+
+void describe_tc_error(int word, char *buf, size_t n) {
+  static const char *const site[] = {"?", "stage-full", "stage-empty", "accumulator-full",
+                                     "accumulator-free"};
+  const int w = word & 15;
+  snprintf(buf, n, "tensor-core panel kernel: bounded wait on the %s barrier ran out (block %d)",
+           site[(w >= 1 && w <= 4) ? w : 0], word >> 4);
+}
+
+vcsr_status launch_tc_panels(const TcView &V0, const float *B, int N, int ldb, float *C,
+                             int ldc, int O, cudaStream_t st, int *launches) {
+  if (launches) *launches = 0;
+  if (V0.n_rb == 0 || O == 0) return VCSR_OK;
+  if (O % 4 || ldb % 4 || ((uintptr_t)B % 16) || ((uintptr_t)C % 4))
+    return fail(VCSR_ERR_UNSUPPORTED,
+                "TF32 panels need O and ldb multiples of 4 and a 16-byte aligned B");
+  EncodeTiledFn enc;
+  VCSR_TRY(encode_fn(&enc));
+  CUtensorMap tm;
+  const cuuint64_t dims[2] = {(cuuint64_t)O, (cuuint64_t)N};
+  const cuuint64_t strides[1] = {(cuuint64_t)ldb * 4};
+  const cuuint32_t box[2] = {32, 16};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)B, dims, strides, box,
+                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(VCSR_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  TcView V = V0;
+  V.O = O;
+  V.ldc = ldc;
+  V.C = C;
+  V.n_ochunks = (int)ceil_div(O, 128);
+  const size_t smem = tc_smem_bytes();
+  VCSR_CUDA(cudaFuncSetAttribute(tc_panel_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem));
+  int dev = 0, sms = 148, per_sm = 1;
+  VCSR_CUDA(cudaGetDevice(&dev));
+  VCSR_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  VCSR_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tc_panel_kernel, kThreads,
+                                                          smem));
+  if (per_sm < 1) per_sm = 1;
+  if (per_sm > 8) per_sm = 8;  // at most 8 x 32 TMEM columns of the SM's 512
+  const long long items = (long long)V.n_rb * V.n_ochunks;
+  long long grid = (long long)sms * per_sm;
+  if (grid > items) grid = items;
+  tc_panel_kernel<<<(int)grid, kThreads, smem, st>>>(V, tm);
+  VCSR_CUDA(cudaGetLastError());
+  if (launches) *launches = 1;
+  return VCSR_OK;
+}
+
+}  // namespace vcsr

@@ -1,0 +1,40 @@
+// spmm_tc.h — the tcgen05 TF32 dense-panel kernel's launch interface.
+#pragma once
+#include <cstddef>
+
+#include <cuda_runtime.h>
+
+#include "common.h"
+
+namespace vcsr {
+
+// Dense 16x16 panels of A on the device.  Row block k (0 <= k < n_rb) starts
+// at row rb_row[k] and owns blocks rb_ptr[k] .. rb_ptr[k+1]-1 (at least one);
+// block b covers columns 16*blk_col[b] .. +15 and its 256 values sit at
+// blk_val + 256*b in the K-major core-matrix order
+//   value(row n, column k) at ((k / 4) * 2 + n / 8) * 32 + (n % 8) * 4 + k % 4,
+// rounded to TF32.
+struct TcView {
+  int n_rb = 0;
+  const int *rb_row = nullptr;
+  const int *rb_ptr = nullptr;
+  const int *blk_col = nullptr;
+  const float *blk_val = nullptr;
+  int M = 0, O = 0, ldc = 0, n_ochunks = 0;
+  float *C = nullptr;
+  // first failure: wait site (1 stage full, 2 stage empty, 3 accumulator
+  // full, 4 accumulator free) | block index << 4; 0 when none
+  int *err = nullptr;
+};
+
+size_t tc_smem_bytes();
+
+// Text for a nonzero error word.
+void describe_tc_error(int word, char *buf, size_t n);
+
+// C[rows of the panels] += panels * B, on `st` (C must already hold the
+// other entries' product).  Needs O and ldb multiples of 4, B 16-byte aligned.
+vcsr_status launch_tc_panels(const TcView &V, const float *B, int N, int ldb, float *C,
+                             int ldc, int O, cudaStream_t st, int *launches);
+
+}  // namespace vcsr

@@ -36,6 +36,7 @@ STATUS = {0: "ok", 1: "invalid", 2: "cuda", 3: "alloc", 4: "io",
           5: "unsupported", 6: "nccl", 7: "timeout", 8: "range"}
 HOST, DEVICE = 0, 1
 PLAN_REFERENCE_FORMAT = 1
+PLAN_TF32_PANELS = 2
 
 
 class VcsrError(RuntimeError):
@@ -68,7 +69,7 @@ class _Vcsr(C.Structure):
 class _PlanParams(C.Structure):
     _fields_ = [("segw", C.c_int), ("bundle", C.c_int), ("tileK", C.c_int),
                 ("max_O", C.c_int), ("vec_rows", C.c_int), ("chunk", C.c_int),
-                ("flags", C.c_int)]
+                ("flags", C.c_int), ("panel_min_nnz", C.c_int)]
 
 
 class _PlanInfo(C.Structure):
@@ -77,7 +78,8 @@ class _PlanInfo(C.Structure):
                 ("num_union", C.c_int64), ("num_units", C.c_int),
                 ("num_split_vectors", C.c_int), ("num_split_units", C.c_int),
                 ("num_long_units", C.c_int), ("panel_bytes", C.c_int64), ("has_reference_format", C.c_int),
-                ("build_ms", C.c_double)]
+                ("build_ms", C.c_double), ("num_panel_blocks", C.c_int),
+                ("num_panel_row_blocks", C.c_int), ("panel_nnz", C.c_int64)]
 
 
 _LIB = None
@@ -110,6 +112,7 @@ _SIGS = {
                             C.c_int, C.c_void_p, C.POINTER(C.c_int)]),
     "vcsr_spmm_host": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
                                  C.c_void_p]),
+    "vcsr_plan_check": (C.c_int, [C.c_void_p, C.c_void_p]),
     "vcsr_spmm_segmented": (C.c_int, [C.POINTER(_Vcsr), C.c_void_p, C.c_int, C.c_int,
                                       C.c_void_p, C.c_void_p]),
     "vcsr_csr_spmm": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
@@ -374,9 +377,9 @@ class DeviceVCSR:
         return _vcsr_from_host_struct(h)
 
     def close(self):
-        if self._s is not None:
-            lib().vcsr_vcsr_free(C.byref(self._s), DEVICE)
-            self._s = None
+        if getattr(self, "_s", None) is not None and _LIB is not None:
+            _LIB.vcsr_vcsr_free(C.byref(self._s), DEVICE)
+        self._s = None
 
     __del__ = close
 
@@ -427,9 +430,9 @@ class CuSparse:
         _check(lib().vcsr_cusparse_run(self._h, _stream(stream)))
 
     def close(self):
-        if self._h:
-            lib().vcsr_cusparse_destroy(self._h)
-            self._h = None
+        if getattr(self, "_h", None) and _LIB is not None:
+            _LIB.vcsr_cusparse_destroy(self._h)
+        self._h = None
 
     __del__ = close
 
@@ -438,13 +441,16 @@ class Plan:
     """Build-once SpMM operator (vcsr_plan_*).  csr is a host CSR or a DeviceCSR."""
 
     def __init__(self, csr, segw=4, bundle=32, tileK=0, max_O=512, vec_rows=0,
-                 chunk=0, reference_format=False, stream=None):
+                 chunk=0, reference_format=False, tf32_panels=False, panel_min_nnz=0,
+                 stream=None):
         L = lib()
         p = _PlanParams()
         L.vcsr_plan_params_default(C.byref(p))
         p.segw, p.bundle, p.tileK, p.max_O = segw, bundle, tileK, max_O
         p.vec_rows, p.chunk = vec_rows, chunk
-        p.flags = PLAN_REFERENCE_FORMAT if reference_format else 0
+        p.flags = ((PLAN_REFERENCE_FORMAT if reference_format else 0)
+                   | (PLAN_TF32_PANELS if tf32_panels else 0))
+        p.panel_min_nnz = panel_min_nnz
         where = DEVICE if isinstance(csr, DeviceCSR) else HOST
         s = csr._struct()
         h = C.c_void_p()
@@ -478,6 +484,11 @@ class Plan:
         self.last_launches = n.value
         return Cout
 
+    def check(self, stream=None):
+        """Synchronise and raise VcsrError (status 7) if a bounded wait of the
+        plan's kernels ran out since the last check."""
+        _check(lib().vcsr_plan_check(self._h, _stream(stream)))
+
     def spmm_host(self, hB, hC, stream=None):
         """C = A*B with host buffers (H2D, SpMM, D2H, synchronise)."""
         O = hB.shape[1] if hB is not None else hC.shape[1]
@@ -485,9 +496,9 @@ class Plan:
         return hC
 
     def close(self):
-        if getattr(self, "_h", None):
-            lib().vcsr_plan_destroy(self._h)
-            self._h = None
+        if getattr(self, "_h", None) and _LIB is not None:
+            _LIB.vcsr_plan_destroy(self._h)
+        self._h = None
 
     __del__ = close
 
@@ -536,8 +547,8 @@ class MultiGPU:
         return out
 
     def close(self):
-        if getattr(self, "_h", None):
-            lib().vcsr_mgpu_destroy(self._h)
-            self._h = None
+        if getattr(self, "_h", None) and _LIB is not None:
+            _LIB.vcsr_mgpu_destroy(self._h)
+        self._h = None
 
     __del__ = close
