@@ -13,6 +13,8 @@ Workloads (synthetic stand-ins with the benchmark configurations' shapes):
                  weak scaling.
   fem_o32 / fem_o512, uniform (O=32), powerlaw_o8 / powerlaw_o64,
   blockdense (O=512): single-panel variants (weak scaling under N GPUs).
+  blockdense_tf32  the same matrix with its dense 16x16 blocks on the
+                 tensor cores in TF32 (VCSR_PLAN_TF32_PANELS).
   rmat           2^22 R-MAT, O = 256: A cut into N nnz-balanced row panels,
                  B broadcast once: strong scaling.
 
@@ -44,8 +46,11 @@ WORKLOADS = {
     "powerlaw_o8": ("powerlaw", 0, 8, "weak", "powerlaw_321821_O8"),
     "powerlaw_o64": ("powerlaw", 0, 64, "weak", "powerlaw_321821_O64"),
     "blockdense": ("blockdense", 0, 512, "weak", "blockdense_65536_O512_fp32"),
+    "blockdense_tf32": ("blockdense", 0, 512, "weak", "blockdense_65536_O512_tf32"),
     "rmat": ("rmat", 22, 256, "strong", "rmat_s22_O256"),
 }
+# workloads whose dense 16x16 blocks run on the tcgen05 TF32 path
+TF32_WORKLOADS = {"blockdense_tf32"}
 
 
 def parse():
@@ -261,7 +266,8 @@ def run_ours(args):
     global_nnz = D.global_nnz(csr, scaling, world, strong_total,
                               dist if world > 1 else None, dev)
     lo = 0.0 if WORKLOADS[args.workload][0] == "rmat" else -1.0
-    plan = V.Plan(csr, segw=4, bundle=32, max_O=max(O, 512))
+    tf32 = args.workload in TF32_WORKLOADS
+    plan = V.Plan(csr, segw=4, bundle=32, max_O=max(O, 512), tf32_panels=tf32)
     info = plan.info()
 
     # B: filled on rank 0, replicated by one NCCL broadcast (timed apart)
@@ -405,13 +411,15 @@ def run_ours(args):
             "metric": METRIC, "value": round(value, 3), "unit": "GFLOP/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms_step, 5), "higher_is_better": True,
-            "scaling": scaling, "vs_baseline": None, "dtype": "f32",
+            "scaling": scaling, "vs_baseline": None, "dtype": "tf32" if tf32 else "f32",
             "data": "synthetic",
             "config": {"workload": label, "M": csr.M, "N": csr.N, "nnz": csr.nnz,
                        "global_nnz": global_nnz, "O": O, "segw": 4, "bundle": 32,
                        "vec_rows": info["vec_rows"], "units": info["num_units"],
                        "split_units": info["num_split_units"],
                        "cols_touched": touched,
+                       "tf32_panel_blocks": info["num_panel_blocks"],
+                       "tf32_panel_nnz": info["panel_nnz"],
                        "l2": "flushed before every timed step (256 MB write)",
                        "parallelism": (f"row panels x{world}, B broadcast once"
                                        if world > 1 else "1 GPU")},

@@ -22,13 +22,16 @@
 // atomics into C) rebuilt with TF32 inputs, FP32 accumulation in TMEM, no
 // atomics, and the O dimension on the tensor core's M side.
 //
-// Roles (160 threads): warps 0-3 read the accumulator (warp w owns TMEM lanes
+// Roles (192 threads): warps 0-3 read the accumulator (warp w owns TMEM lanes
 // 32w..32w+31) and add it into C; warp 4 allocates TMEM and its lane 0 issues
-// the TMA loads (an S-stage ring, `full`/`empty` mbarriers) and the MMAs.
-// Two accumulators alternate between items so the epilogue of item t runs
-// while the MMAs of item t+1 are issued.  Every mbarrier wait is bounded:
-// after ~2^22 polls the kernel records which wait gave up, stops and frees
-// its TMEM.
+// the TMA loads into an 8-stage ring (`full`/`empty` mbarriers); lane 0 of
+// warp 5 issues the MMAs.  The producer runs up to 8 blocks ahead of the
+// MMAs, so a CTA keeps 8 B slabs in flight (3 CTAs per SM).  Two
+// accumulators alternate between items so the epilogue of item t runs while
+// the MMAs of item t+1 are issued.  Every mbarrier wait is bounded: after
+// ~2^22 polls the kernel records which wait gave up and stops; before it
+// frees its TMEM and exits it still waits (bounded) for its issued MMAs and
+// for the copies it issued but did not consume.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -41,16 +44,19 @@
 namespace vcsr {
 namespace {
 
-constexpr int kStages = 4;
+constexpr int kStages = 8;
 constexpr int kBTileBytes = 16 * 128 * 4;  // 16 rows x 128 floats, 4 swizzled boxes
 constexpr int kABlockBytes = 16 * 16 * 4;  // one dense block
 constexpr int kStageBytes = kBTileBytes + kABlockBytes;
-constexpr int kThreads = 160;
+constexpr int kThreads = 192;
+constexpr int kProducerWarp = 4, kMmaWarp = 5;
 constexpr uint32_t kTmemCols = 32;  // two 16-column accumulators
 constexpr long long kPollLimit = 1ll << 22;
 
 // Where a bounded wait gave up (recorded in the plan's error word).
-enum WaitSite : int { kWaitFull = 1, kWaitEmpty = 2, kWaitAccFull = 3, kWaitAccFree = 4 };
+enum WaitSite : int {
+  kWaitFull = 1, kWaitEmpty = 2, kWaitAccFull = 3, kWaitAccFree = 4, kWaitDrain = 5
+};
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return (uint32_t)__cvta_generic_to_shared(p);
@@ -140,10 +146,6 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar) {
       : "memory");
 }
 
-struct ItemCursor {  // walks (item, block) pairs of this CTA in order
-  int item, blk, nblk, rbi, oc;
-};
-
 __global__ void __launch_bounds__(kThreads, 1)
     tc_panel_kernel(const TcView V, const __grid_constant__ CUtensorMap tmB) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -155,8 +157,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t *full = bars, *empty = bars + kStages;
   uint64_t *dfull = bars + 2 * kStages;      // accumulator b ready (count 1)
   uint64_t *dfree = bars + 2 * kStages + 2;  // accumulator b read (count 128)
-  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 2 * kStages + 4);
+  uint64_t *drain = bars + 2 * kStages + 4;  // all MMAs of this CTA done
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 2 * kStages + 5);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+  long long *consumed = reinterpret_cast<long long *>(bars + 2 * kStages + 6);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -168,10 +172,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(dfull + b, 1);
       mbar_init(dfree + b, 128);
     }
+    mbar_init(drain, 1);
     *abort_flag = 0;
+    *consumed = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 4) {  // one warp allocates the accumulators
+  if (warp == kProducerWarp) {  // one warp allocates the accumulators
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_holder)),
                  "r"(kTmemCols));
@@ -182,45 +188,39 @@ __global__ void __launch_bounds__(kThreads, 1)
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_holder;
   const int n_items = V.n_rb * V.n_ochunks;
+  long long g_load = 0;  // producer: stages issued
 
-  if (warp == 4) {
+  if (warp == kProducerWarp) {
     if (lane == 0) {
-      // ---------------------------------------------- producer + MMA issue
-      auto item_of = [&](int t, ItemCursor &c) {
-        c.item = t;
-        c.blk = 0;
-        c.oc = t / V.n_rb;
-        c.rbi = t - c.oc * V.n_rb;
-        c.nblk = V.rb_ptr[c.rbi + 1] - V.rb_ptr[c.rbi];
-      };
-      ItemCursor ld;  // next (item, block) to load
-      item_of(blockIdx.x, ld);
-      long long g_load = 0, g_mma = 0;  // stages loaded / consumed so far
-      auto issue_load = [&]() -> bool {  // loads the next stage, false at the end
-        while (ld.item < n_items && ld.blk >= ld.nblk) item_of(ld.item + gridDim.x, ld);
-        if (ld.item >= n_items) return false;
-        const int s = (int)(g_load % kStages);
-        if (g_load >= kStages &&
-            !mbar_wait(empty + s, (uint32_t)(((g_load / kStages) - 1) & 1), abort_flag,
-                       kWaitEmpty))
-          return false;
-        unsigned char *st = stage + s * kStageBytes;
-        const int bi = V.rb_ptr[ld.rbi] + ld.blk;
-        const int j = V.blk_col[bi];
-        mbar_expect_tx(full + s, kStageBytes);
-        bulk_load(st + kBTileBytes, V.blk_val + (size_t)bi * 256, kABlockBytes, full + s);
+      // ------------------------------------------------ TMA producer
+      for (int t = blockIdx.x; t < n_items && !*abort_flag; t += gridDim.x) {
+        const int oc = t / V.n_rb, rbi = t - oc * V.n_rb;
+        const int b0 = V.rb_ptr[rbi], b1 = V.rb_ptr[rbi + 1];
+        for (int bi = b0; bi < b1; ++bi) {
+          const int s = (int)(g_load % kStages);
+          if (g_load >= kStages &&
+              !mbar_wait(empty + s, (uint32_t)(((g_load / kStages) - 1) & 1), abort_flag,
+                         kWaitEmpty))
+            break;
+          unsigned char *st = stage + s * kStageBytes;
+          const int j = V.blk_col[bi];
+          mbar_expect_tx(full + s, kStageBytes);
+          bulk_load(st + kBTileBytes, V.blk_val + (size_t)bi * 256, kABlockBytes, full + s);
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-          tma_load_2d(st + q * 2048, &tmB, ld.oc * 128 + 32 * q, 16 * j, full + s);
-        ++ld.blk;
-        ++g_load;
-        return true;
-      };
-      for (int s = 0; s < kStages - 1; ++s)
-        if (!issue_load()) break;
+          for (int q = 0; q < 4; ++q)
+            tma_load_2d(st + q * 2048, &tmB, oc * 128 + 32 * q, 16 * j, full + s);
+          ++g_load;
+        }
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    if (lane == 0) {
+      // ------------------------------------------------ MMA issue
+      long long g = 0;
       int lt = 0;  // local item count
       for (int t = blockIdx.x; t < n_items && !*abort_flag; t += gridDim.x, ++lt) {
         const int oc = t / V.n_rb, rbi = t - oc * V.n_rb;
+        (void)oc;
         const int nblk = V.rb_ptr[rbi + 1] - V.rb_ptr[rbi];
         const int buf = lt & 1;
         if (lt >= 2 && !mbar_wait(dfree + buf, (uint32_t)(((lt - 2) >> 1) & 1), abort_flag,
@@ -228,12 +228,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t dt = tmem + (uint32_t)(buf * 16);
+        bool ok = true;
         for (int b = 0; b < nblk; ++b) {
-          const int s = (int)(g_mma % kStages);
-          if (!mbar_wait(full + s, (uint32_t)((g_mma / kStages) & 1), abort_flag, kWaitFull))
+          const int s = (int)(g % kStages);
+          if (!mbar_wait(full + s, (uint32_t)((g / kStages) & 1), abort_flag, kWaitFull)) {
+            ok = false;
             break;
-          unsigned char *st = stage + s * kStageBytes;
-          const uint32_t a_addr = smem_u32(st), b_addr = smem_u32(st + kBTileBytes);
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t a_addr = smem_u32(stage + s * kStageBytes);
+          const uint32_t b_addr = a_addr + kBTileBytes;
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             // A: MN atoms (32 floats) 2048 bytes apart (one TMA box each),
@@ -244,11 +248,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_tf32(dt, ad, bd, (b > 0 || h > 0) ? 1u : 0u);
           }
           mma_commit(empty + s);
-          ++g_mma;
-          issue_load();  // refill: waits for the MMA of an older stage
+          ++g;
         }
+        if (!ok) break;
         mma_commit(dfull + buf);  // the plan lists only row blocks with dense blocks
       }
+      *consumed = g;
+      // every MMA issued by this thread has finished before TMEM is freed
+      mma_commit(drain);
+      volatile int no_abort = 0;  // wait even when another role gave up
+      if (!mbar_wait(drain, 0, &no_abort, kWaitDrain)) *abort_flag = kWaitDrain;
     }
   } else {
     // -------------------------------------------------------- epilogue
@@ -273,21 +282,32 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m = oc * 128 + warp * 32 + lane;  // column of C
       const int row0 = V.rb_row[rbi];
       if (m < V.O) {
+        float *c = V.C + (size_t)row0 * V.ldc + m;
+        const int nrow = min(16, V.M - row0);
+        float cv[16];
 #pragma unroll
-        for (int n = 0; n < 16; ++n) {
-          const int row = row0 + n;
-          if (row < V.M) {
-            float *c = V.C + (size_t)row * V.ldc + m;
-            *c += __uint_as_float(r[n]);
-          }
-        }
+        for (int n = 0; n < 16; ++n)
+          if (n < nrow) cv[n] = c[(size_t)n * V.ldc];
+#pragma unroll
+        for (int n = 0; n < 16; ++n)
+          if (n < nrow) c[(size_t)n * V.ldc] = cv[n] + __uint_as_float(r[n]);
       }
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
+  if (warp == kProducerWarp && lane == 0 && *abort_flag) {
+    // copies issued but never consumed must land before the CTA exits
+    for (long long g = *consumed; g < g_load; ++g) {
+      volatile int no_abort = 0;
+      if (!mbar_wait(full + (int)(g % kStages), (uint32_t)((g / kStages) & 1), &no_abort,
+                     kWaitFull))
+        break;
+    }
+  }
   if (threadIdx.x == 0 && *abort_flag) atomicCAS(V.err, 0, *abort_flag | (int)(blockIdx.x << 4));
-  if (warp == 4) {
+  __syncwarp();
+  if (warp == kProducerWarp) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"(kTmemCols));
@@ -322,11 +342,11 @@ vcsr_status encode_fn(EncodeTiledFn *out) {
 size_t tc_smem_bytes() { return (size_t)kStages * kStageBytes + 1024 + 256; }
 
 void describe_tc_error(int word, char *buf, size_t n) {
-  static const char *const site[] = {"?", "stage-full", "stage-empty", "accumulator-full",
-                                     "accumulator-free"};
+  static const char *const site[] = {"?",          "stage-full",       "stage-empty",
+                                     "accumulator-full", "accumulator-free", "MMA-drain"};
   const int w = word & 15;
   snprintf(buf, n, "tensor-core panel kernel: bounded wait on the %s barrier ran out (block %d)",
-           site[(w >= 1 && w <= 4) ? w : 0], word >> 4);
+           site[(w >= 1 && w <= 5) ? w : 0], word >> 4);
 }
 
 vcsr_status launch_tc_panels(const TcView &V0, const float *B, int N, int ldb, float *C,
@@ -358,10 +378,14 @@ vcsr_status launch_tc_panels(const TcView &V0, const float *B, int N, int ldb, f
   int dev = 0, sms = 148, per_sm = 1;
   VCSR_CUDA(cudaGetDevice(&dev));
   VCSR_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  VCSR_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tc_panel_kernel, kThreads,
-                                                          smem));
+  // resident CTAs per SM from shared memory (each also holds kTmemCols of
+  // the SM's 512 TMEM columns)
+  int smem_sm = 0, smem_reserved = 0;
+  VCSR_CUDA(cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev));
+  VCSR_CUDA(cudaDeviceGetAttribute(&smem_reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev));
+  per_sm = (int)(smem_sm / (smem + (size_t)smem_reserved));
   if (per_sm < 1) per_sm = 1;
-  if (per_sm > 8) per_sm = 8;  // at most 8 x 32 TMEM columns of the SM's 512
+  if (per_sm > (int)(512 / kTmemCols)) per_sm = (int)(512 / kTmemCols);
   const long long items = (long long)V.n_rb * V.n_ochunks;
   long long grid = (long long)sms * per_sm;
   if (grid > items) grid = items;
