@@ -24,9 +24,11 @@
 //
 // Roles (192 threads): warps 0-3 read the accumulator (warp w owns TMEM lanes
 // 32w..32w+31) and add it into C; warp 4 allocates TMEM and its lane 0 issues
-// the TMA loads into an 8-stage ring (`full`/`empty` mbarriers); lane 0 of
-// warp 5 issues the MMAs.  The producer runs up to 8 blocks ahead of the
-// MMAs, so a CTA keeps 8 B slabs in flight (3 CTAs per SM).  Two
+// the copies into a ring of stages of kG blocks each (`full`/`empty`
+// mbarriers); lane 0 of warp 5 issues the MMAs.  The producer runs up to
+// kStages * kG blocks ahead of the MMAs.  Measured on B200 the copy issue
+// rate of the SM's TMA unit (about 46 cycles per 2-KB box) bounds this
+// kernel; grouping blocks per stage saves barrier round trips.  Two
 // accumulators alternate between items so the epilogue of item t runs while
 // the MMAs of item t+1 are issued.  Every mbarrier wait is bounded: after
 // ~2^22 polls the kernel records which wait gave up and stops; before it
@@ -44,10 +46,20 @@
 namespace vcsr {
 namespace {
 
-constexpr int kStages = 8;
+#ifndef VCSR_TC_BLOCKS_PER_STAGE
+#define VCSR_TC_BLOCKS_PER_STAGE 4
+#endif
+#ifndef VCSR_TC_STAGES
+#define VCSR_TC_STAGES 2
+#endif
+// A stage holds kG dense blocks with their B slabs: one full/empty round
+// trip (copies landing, MMA issue, MMA completion) per kG blocks.
+constexpr int kG = VCSR_TC_BLOCKS_PER_STAGE;
+constexpr int kStages = VCSR_TC_STAGES;
 constexpr int kBTileBytes = 16 * 128 * 4;  // 16 rows x 128 floats, 4 swizzled boxes
 constexpr int kABlockBytes = 16 * 16 * 4;  // one dense block
-constexpr int kStageBytes = kBTileBytes + kABlockBytes;
+constexpr int kBlockBytes = kBTileBytes + kABlockBytes;
+constexpr int kStageBytes = kG * kBlockBytes;  // slabs first, then the blocks
 constexpr int kThreads = 192;
 constexpr int kProducerWarp = 4, kMmaWarp = 5;
 constexpr uint32_t kTmemCols = 32;  // two 16-column accumulators
@@ -66,8 +78,9 @@ __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
 }
 
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+// Adds to the transaction count of the current phase (no arrival).
+__device__ __forceinline__ void mbar_add_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)),
                "r"(bytes)
                : "memory");
 }
@@ -188,30 +201,43 @@ __global__ void __launch_bounds__(kThreads, 1)
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_holder;
   const int n_items = V.n_rb * V.n_ochunks;
-  long long g_load = 0;  // producer: stages issued
+  long long g_load = 0;  // producer: blocks issued
 
   if (warp == kProducerWarp) {
     if (lane == 0) {
       // ------------------------------------------------ TMA producer
+      // block g goes to slot g % kG of stage (g / kG) % kStages; each block
+      // adds its bytes to the stage's transaction count and the last block
+      // of a stage (or of this CTA's work) arrives on it
       for (int t = blockIdx.x; t < n_items && !*abort_flag; t += gridDim.x) {
         const int oc = t / V.n_rb, rbi = t - oc * V.n_rb;
         const int b0 = V.rb_ptr[rbi], b1 = V.rb_ptr[rbi + 1];
+        bool ok = true;
         for (int bi = b0; bi < b1; ++bi) {
-          const int s = (int)(g_load % kStages);
-          if (g_load >= kStages &&
-              !mbar_wait(empty + s, (uint32_t)(((g_load / kStages) - 1) & 1), abort_flag,
-                         kWaitEmpty))
+          const int u = (int)(g_load % kG);
+          const long long sidx = g_load / kG;
+          const int s = (int)(sidx % kStages);
+          if (u == 0 && sidx >= kStages &&
+              !mbar_wait(empty + s, (uint32_t)(((sidx / kStages) - 1) & 1), abort_flag,
+                         kWaitEmpty)) {
+            ok = false;
             break;
+          }
           unsigned char *st = stage + s * kStageBytes;
           const int j = V.blk_col[bi];
-          mbar_expect_tx(full + s, kStageBytes);
-          bulk_load(st + kBTileBytes, V.blk_val + (size_t)bi * 256, kABlockBytes, full + s);
+          mbar_add_tx(full + s, kBlockBytes);
+          bulk_load(st + kG * kBTileBytes + u * kABlockBytes, V.blk_val + (size_t)bi * 256,
+                    kABlockBytes, full + s);
 #pragma unroll
           for (int q = 0; q < 4; ++q)
-            tma_load_2d(st + q * 2048, &tmB, oc * 128 + 32 * q, 16 * j, full + s);
+            tma_load_2d(st + u * kBTileBytes + q * 2048, &tmB, oc * 128 + 32 * q, 16 * j,
+                        full + s);
           ++g_load;
+          if (u == kG - 1) mbar_arrive(full + s);
         }
+        if (!ok) break;
       }
+      if (g_load % kG) mbar_arrive(full + (int)((g_load / kG) % kStages));  // partial stage
     }
   } else if (warp == kMmaWarp) {
     if (lane == 0) {
@@ -230,14 +256,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t dt = tmem + (uint32_t)(buf * 16);
         bool ok = true;
         for (int b = 0; b < nblk; ++b) {
-          const int s = (int)(g % kStages);
-          if (!mbar_wait(full + s, (uint32_t)((g / kStages) & 1), abort_flag, kWaitFull)) {
-            ok = false;
-            break;
+          const int u = (int)(g % kG);
+          const long long sidx = g / kG;
+          const int s = (int)(sidx % kStages);
+          if (u == 0) {
+            if (!mbar_wait(full + s, (uint32_t)((sidx / kStages) & 1), abort_flag, kWaitFull)) {
+              ok = false;
+              break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           }
-          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const uint32_t a_addr = smem_u32(stage + s * kStageBytes);
-          const uint32_t b_addr = a_addr + kBTileBytes;
+          const uint32_t a_addr = smem_u32(stage + s * kStageBytes + u * kBTileBytes);
+          const uint32_t b_addr =
+              smem_u32(stage + s * kStageBytes + kG * kBTileBytes + u * kABlockBytes);
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             // A: MN atoms (32 floats) 2048 bytes apart (one TMA box each),
@@ -247,13 +278,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t bd = smem_desc(b_addr + h * 512, 256, 128, 0);
             mma_tf32(dt, ad, bd, (b > 0 || h > 0) ? 1u : 0u);
           }
-          mma_commit(empty + s);
           ++g;
+          if (u == kG - 1) mma_commit(empty + s);
         }
         if (!ok) break;
         mma_commit(dfull + buf);  // the plan lists only row blocks with dense blocks
       }
-      *consumed = g;
+      *consumed = (g + kG - 1) / kG;  // stages whose copies were waited for
       // every MMA issued by this thread has finished before TMEM is freed
       mma_commit(drain);
       volatile int no_abort = 0;  // wait even when another role gave up
@@ -298,7 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == kProducerWarp && lane == 0 && *abort_flag) {
     // copies issued but never consumed must land before the CTA exits
-    for (long long g = *consumed; g < g_load; ++g) {
+    for (long long g = *consumed; g < (g_load + kG - 1) / kG; ++g) {
       volatile int no_abort = 0;
       if (!mbar_wait(full + (int)(g % kStages), (uint32_t)((g / kStages) & 1), &no_abort,
                      kWaitFull))
