@@ -110,3 +110,22 @@ def test_tf32_panels_need_aligned_o():
     with pytest.raises(V.VcsrError) as ei:
         plan.spmm(dB, dC)
     assert ei.value.status == 5
+
+
+def test_cli_vcsr_tc():
+    """spmm_vcsr --algo vcsr_tc runs the TF32 panel path and prints the
+    'Name: <ms> ms <gflops> GFLOP/s [..]' line; with O % 4 != 0 it reports N/A."""
+    import os
+    import subprocess
+    from helpers import ROOT
+    exe = os.path.join(ROOT, "vcsr-spmm_b200", "bin", "spmm_vcsr")
+    out = subprocess.run([exe, "--gen", "blockdense", "--size", "2048", "--O", "64",
+                          "--algo", "vcsr_tc", "--repeat", "2"],
+                         capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0, out.stderr
+    last = out.stdout.strip().splitlines()[-1]
+    assert last.startswith("VCSR_TC:") and "GFLOP/s" in last and "panels=" in last
+    na = subprocess.run([exe, "--gen", "blockdense", "--size", "1024", "--O", "30",
+                         "--algo", "vcsr_tc", "--repeat", "2"],
+                        capture_output=True, text=True, timeout=120)
+    assert na.returncode == 0 and "N/A" in na.stdout

@@ -292,7 +292,29 @@ int main(int argc, char **argv) {
     report("VCSR (seg)", "VCSR (seg)", ms, note, fetch());
     vcsr_vcsr_free(&v, VCSR_DEVICE);
   }
-  for (const char *na : {"vcsr_naive", "fast", "vcsr_tc"})
+  if (all || algo == "vcsr_tc") {  // dense 16x16 blocks on the tensor cores (TF32)
+    if (O % 4) {
+      printf("%-16s %10s %12s (TF32 panels need O %% 4 == 0)\n", "VCSR_TC", "N/A", "N/A");
+    } else {
+      vcsr_plan_params p;
+      vcsr_plan_params_default(&p);
+      p.segw = segw; p.bundle = bundle; p.tileK = tileK; p.max_O = std::max(O, 512);
+      p.flags = VCSR_PLAN_TF32_PANELS;
+      vcsr_plan *plan = nullptr;
+      vcsr_csr view = as_view(csr);
+      VK(vcsr_plan_create(&view, VCSR_HOST, &p, &plan, st));
+      vcsr_plan_info info{};
+      VK(vcsr_plan_get_info(plan, &info));
+      double ms = timed([&] { VK(vcsr_spmm(plan, dB, O, dC, O, O, st, nullptr)); }, false);
+      VK(vcsr_plan_check(plan, st));
+      char note[256];
+      snprintf(note, sizeof note, "tcgen05 TF32 panels=%d (%lld nnz),residual vec_rows=%d",
+               info.num_panel_blocks, (long long)info.panel_nnz, info.vec_rows);
+      report("VCSR_TC (TF32)", "VCSR_TC", ms, note, fetch());
+      vcsr_plan_destroy(plan);
+    }
+  }
+  for (const char *na : {"vcsr_naive", "fast"})
     if (algo == na) printf("%-16s %10s %12s (not provided by this engine)\n", na, "N/A", "N/A");
   printf("\n");
   for (auto &s : summary) printf("%s\n", s.c_str());
