@@ -216,7 +216,11 @@ vcsr_status vcsr_spmm(const vcsr_plan *plan, const float *dB, int ldb,
 
 /* The same product with host buffers: copies hB (N x O, ld = O) to the device,
  * runs vcsr_spmm, copies C back to hC (M x O, ld = O) and synchronises the
- * stream.  Host buffers should be pinned for full PCIe speed. */
+ * stream.  Replaces the upload/launch/download sequence of the reference's
+ * main (src/main.cpp:104-161) as one call.  With more than 8 MB of B and C
+ * and O >= 128 it pipelines up to four column chunks: chunk k's download (on
+ * a plan-owned stream) overlaps chunk k+1's upload (on `stream`).  Host
+ * buffers should be pinned for full PCIe speed and for the overlap. */
 vcsr_status vcsr_spmm_host(vcsr_plan *plan, const float *hB, float *hC, int O,
                            vcsr_stream_t stream);
 

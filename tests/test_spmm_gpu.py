@@ -191,6 +191,30 @@ def test_device_csr_input_and_host_entry_point():
     assert np.array_equal(C, C2)
 
 
+@pytest.mark.parametrize("O,pinned", [(128, True), (200, True), (256, False)])
+def test_host_entry_point_pipelined(O, pinned):
+    """Above 8 MB of B and C the host entry point runs column chunks as an
+    upload / multiply / download pipeline on two streams; the result equals
+    the device entry point's, run after run, pinned host memory or not."""
+    csr = V.gen_csr("fem", 0)
+    B = V.gen_dense_host(csr.N, O, 5)
+    plan = V.Plan(csr)
+    dC = torch.empty(csr.M, O, device="cuda")
+    plan.spmm(torch.from_numpy(B).cuda(), dC)
+    ref = dC.cpu().numpy()
+    if pinned:
+        hB = torch.from_numpy(B).pin_memory()
+        hC = torch.full((csr.M, O), float("nan")).pin_memory()
+        Bn, Cn = hB.numpy(), hC.numpy()
+    else:
+        Bn, Cn = B, np.full((csr.M, O), np.nan, np.float32)
+    for _ in range(2):
+        Cn[...] = np.nan
+        plan.spmm_host(Bn, Cn)
+        assert rel_l2(Cn, ref) <= 1e-6
+        assert np.array_equal(Cn, ref)  # FEM has no split or long units: same sums
+
+
 def test_full_fem_o128_against_oracle():
     """The bench workload at full size, checked element-wise."""
     csr = V.gen_csr("fem", 0)

@@ -53,8 +53,11 @@ struct vcsr_plan {
   // side stream and events for running long units beside short ones
   cudaStream_t side = nullptr;
   cudaEvent_t fork = nullptr, join = nullptr;
-  // host-buffer entry point staging
+  // host-buffer entry point: staging buffers, the download stream and one
+  // event per column chunk
   float *d_stage_B = nullptr, *d_stage_C = nullptr;
+  cudaStream_t down = nullptr;
+  std::vector<cudaEvent_t> chunk_done;
   size_t stage_B = 0, stage_C = 0;
   double build_ms = 0;
 };
@@ -82,6 +85,8 @@ void release(vcsr_plan *p) {
   cudaFree(p->d_rb_row); cudaFree(p->d_rb_ptr); cudaFree(p->d_blk_col);
   cudaFree(p->d_blk_val); cudaFree(p->d_err);
   if (p->side) cudaStreamDestroy(p->side);
+  if (p->down) cudaStreamDestroy(p->down);
+  for (cudaEvent_t e : p->chunk_done) cudaEventDestroy(e);
   if (p->fork) cudaEventDestroy(p->fork);
   if (p->join) cudaEventDestroy(p->join);
 }
@@ -501,10 +506,61 @@ vcsr_status vcsr_spmm_host(vcsr_plan *p, const float *hB, float *hC, int O,
     VCSR_CUDA(cudaMalloc(&p->d_stage_C, nc));
     p->stage_C = nc;
   }
-  if (nb) VCSR_CUDA(cudaMemcpyAsync(p->d_stage_B, hB, nb, cudaMemcpyHostToDevice, st));
-  VCSR_TRY(vcsr_spmm(p, p->d_stage_B, O, p->d_stage_C, O, O, stream, nullptr));
-  if (nc) VCSR_CUDA(cudaMemcpyAsync(hC, p->d_stage_C, nc, cudaMemcpyDeviceToHost, st));
-  VCSR_CUDA(cudaStreamSynchronize(st));
+  // Columns of B and C split into chunks are independent products
+  // (C[:, chunk] = A * B[:, chunk]).  With large buffers the call runs as a
+  // pipeline of up to four chunks: chunk k is uploaded and multiplied on
+  // `stream`, then downloaded on the plan's download stream while chunk k+1
+  // is uploaded, so the two PCIe directions overlap.  Chunk copies are 2-D
+  // (w floats out of every row of O); measured on B200 hosts, rows of at
+  // least 256 bytes keep both directions at full speed (128-byte rows lose
+  // a third), so a chunk is at least 64 floats wide.
+  constexpr size_t kPipelineBytes = (size_t)8 << 20;
+  int W = O;
+  if (O >= 128 && nb + nc >= kPipelineBytes) {
+    const int nch = std::min(4, O / 64);
+    W = (int)(((O + nch - 1) / nch + 3) & ~3);
+  }
+  const int n_chunks = O > 0 ? (O + W - 1) / W : 0;
+  if (n_chunks <= 1) {
+    if (nb) VCSR_CUDA(cudaMemcpyAsync(p->d_stage_B, hB, nb, cudaMemcpyHostToDevice, st));
+    VCSR_TRY(vcsr_spmm(p, p->d_stage_B, O, p->d_stage_C, O, O, stream, nullptr));
+    if (nc) VCSR_CUDA(cudaMemcpyAsync(hC, p->d_stage_C, nc, cudaMemcpyDeviceToHost, st));
+    VCSR_CUDA(cudaStreamSynchronize(st));
+    return p->d_err ? vcsr_plan_check(p, stream) : VCSR_OK;
+  }
+  if (!p->down) VCSR_CUDA(cudaStreamCreateWithFlags(&p->down, cudaStreamNonBlocking));
+  while ((int)p->chunk_done.size() < n_chunks) {
+    cudaEvent_t e;
+    VCSR_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    p->chunk_done.push_back(e);
+  }
+  const size_t pitch = sizeof(float) * (size_t)O;
+  vcsr_status status = VCSR_OK;
+  for (int k = 0; k < n_chunks && status == VCSR_OK; ++k) {
+    const int o0 = k * W, w = std::min(W, O - o0);
+    cudaError_t e = cudaSuccess;
+    if (p->N > 0)
+      e = cudaMemcpy2DAsync(p->d_stage_B + o0, pitch, hB + o0, pitch, sizeof(float) * w,
+                            (size_t)p->N, cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) {
+      status = fail(VCSR_ERR_CUDA, "chunk upload: %s", cudaGetErrorString(e));
+      break;
+    }
+    status = vcsr_spmm(p, p->d_stage_B + o0, O, p->d_stage_C + o0, O, w, stream, nullptr);
+    if (status != VCSR_OK) break;
+    e = cudaEventRecord(p->chunk_done[k], st);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(p->down, p->chunk_done[k], 0);
+    if (e == cudaSuccess && p->M > 0)
+      e = cudaMemcpy2DAsync(hC + o0, pitch, p->d_stage_C + o0, pitch, sizeof(float) * w,
+                            (size_t)p->M, cudaMemcpyDeviceToHost, p->down);
+    if (e != cudaSuccess) status = fail(VCSR_ERR_CUDA, "chunk download: %s", cudaGetErrorString(e));
+  }
+  // both streams drain before returning, also after an error
+  const cudaError_t e1 = cudaStreamSynchronize(p->down), e2 = cudaStreamSynchronize(st);
+  if (status != VCSR_OK) return status;
+  if (e1 != cudaSuccess || e2 != cudaSuccess)
+    return fail(VCSR_ERR_CUDA, "host entry point: %s",
+                cudaGetErrorString(e1 != cudaSuccess ? e1 : e2));
   return p->d_err ? vcsr_plan_check(p, stream) : VCSR_OK;
 }
 
