@@ -218,9 +218,14 @@ vcsr_status vcsr_spmm(const vcsr_plan *plan, const float *dB, int ldb,
  * runs vcsr_spmm, copies C back to hC (M x O, ld = O) and synchronises the
  * stream.  Replaces the upload/launch/download sequence of the reference's
  * main (src/main.cpp:104-161) as one call.  With more than 8 MB of B and C
- * and O >= 128 it pipelines up to four column chunks: chunk k's download (on
- * a plan-owned stream) overlaps chunk k+1's upload (on `stream`).  Host
- * buffers should be pinned for full PCIe speed and for the overlap. */
+ * the transfers overlap the work: for banded matrices (every row panel reads
+ * B rows of at most the next upload chunk) B goes up in row chunks, each row
+ * panel runs as soon as its B rows are on the device and its C rows come
+ * back while later chunks go up; otherwise, with O >= 128, up to four column
+ * chunks form the pipeline (chunk k comes back while chunk k+1 goes up).
+ * Downloads and products run on plan-owned streams; the call returns after
+ * all of them.  Host buffers should be pinned for full PCIe speed and for
+ * the overlap. */
 vcsr_status vcsr_spmm_host(vcsr_plan *plan, const float *hB, float *hC, int O,
                            vcsr_stream_t stream);
 

@@ -56,8 +56,15 @@ struct vcsr_plan {
   // host-buffer entry point: staging buffers, the download stream and one
   // event per column chunk
   float *d_stage_B = nullptr, *d_stage_C = nullptr;
-  cudaStream_t down = nullptr;
+  cudaStream_t down = nullptr, comp = nullptr;
   std::vector<cudaEvent_t> chunk_done;
+  // row panels for the host entry point's row pipeline: vectors
+  // [v0, v1) = batches [b0, b1) + long units [l0, l1); the panel's rows read
+  // B rows up to col_max
+  struct RowPanel {
+    int row0, row1, b0, b1, l0, l1, col_max;
+  };
+  std::vector<RowPanel> rpanels;
   size_t stage_B = 0, stage_C = 0;
   double build_ms = 0;
 };
@@ -86,6 +93,7 @@ void release(vcsr_plan *p) {
   cudaFree(p->d_blk_val); cudaFree(p->d_err);
   if (p->side) cudaStreamDestroy(p->side);
   if (p->down) cudaStreamDestroy(p->down);
+  if (p->comp) cudaStreamDestroy(p->comp);
   for (cudaEvent_t e : p->chunk_done) cudaEventDestroy(e);
   if (p->fork) cudaEventDestroy(p->fork);
   if (p->join) cudaEventDestroy(p->join);
@@ -333,6 +341,44 @@ vcsr_status vcsr_plan_create(const vcsr_csr *csr, int csr_where,
   }
   p->n_batches = (int)batches.size();
   p->n_long = (int)long_idx.size();
+  // Row panels (about equal nnz, cut at vectors where a batch or a long unit
+  // starts) for the host entry point's row pipeline; not with TF32 panels,
+  // whose kernel covers all rows at once.
+  if (p->n_panel_rb == 0 && work.M >= 8192 && work.nnz >= (1 << 20)) {
+    constexpr int kRowPanels = 8;
+    std::vector<int> cuts;  // vector indices where a panel may start
+    for (const int4 &b : batches) cuts.push_back(b.x);
+    for (int u : long_idx) cuts.push_back(ph.units[u].vec);
+    std::sort(cuts.begin(), cuts.end());
+    cuts.erase(std::unique(cuts.begin(), cuts.end()), cuts.end());
+    std::vector<int> vb{0};
+    for (int j = 1; j < kRowPanels; ++j) {
+      const int64_t target = (int64_t)work.nnz * j / kRowPanels;
+      const int row = (int)(std::lower_bound(work.row_ptr, work.row_ptr + work.M + 1, target) -
+                            work.row_ptr);
+      auto it = std::lower_bound(cuts.begin(), cuts.end(), row / ph.R);
+      if (it != cuts.end() && *it > vb.back()) vb.push_back(*it);
+    }
+    vb.push_back(ph.num_vectors);
+    std::vector<int> lvec(long_idx.size());
+    for (size_t i = 0; i < long_idx.size(); ++i) lvec[i] = ph.units[long_idx[i]].vec;
+    std::vector<int> bvec(batches.size());
+    for (size_t i = 0; i < batches.size(); ++i) bvec[i] = batches[i].x;
+    for (size_t j = 0; j + 1 < vb.size(); ++j) {
+      vcsr_plan::RowPanel rp;
+      rp.row0 = vb[j] * ph.R;
+      rp.row1 = std::min(work.M, vb[j + 1] * ph.R);
+      rp.b0 = (int)(std::lower_bound(bvec.begin(), bvec.end(), vb[j]) - bvec.begin());
+      rp.b1 = (int)(std::lower_bound(bvec.begin(), bvec.end(), vb[j + 1]) - bvec.begin());
+      rp.l0 = (int)(std::lower_bound(lvec.begin(), lvec.end(), vb[j]) - lvec.begin());
+      rp.l1 = (int)(std::lower_bound(lvec.begin(), lvec.end(), vb[j + 1]) - lvec.begin());
+      rp.col_max = -1;
+      for (int r = rp.row0; r < rp.row1; ++r)
+        if (work.row_ptr[r + 1] > work.row_ptr[r])
+          rp.col_max = std::max(rp.col_max, work.col[work.row_ptr[r + 1] - 1]);
+      p->rpanels.push_back(rp);
+    }
+  }
   std::vector<int2> parts(ph.parts.size()), svecs(ph.svecs.size());
   std::memcpy(parts.data(), ph.parts.data(), sizeof(int2) * parts.size());
   std::memcpy(svecs.data(), ph.svecs.data(), sizeof(int2) * svecs.size());
@@ -506,6 +552,74 @@ vcsr_status vcsr_spmm_host(vcsr_plan *p, const float *hB, float *hC, int O,
     VCSR_CUDA(cudaMalloc(&p->d_stage_C, nc));
     p->stage_C = nc;
   }
+  constexpr size_t kPipelineBytes = (size_t)8 << 20;
+  if (O > 0 && p->N > 0 && p->M > 0 && nb + nc >= kPipelineBytes && !p->rpanels.empty() &&
+      !(p->n_split_units > 0 && O > p->pstride)) {
+    // Row pipeline for banded matrices: B goes up in K contiguous row chunks
+    // on `stream`; row panel j runs on the plan's compute stream once the
+    // chunk holding its highest column is up, and its C rows go back on the
+    // download stream.  Used when every panel reads B rows of at most the
+    // next chunk, so uploads, products and downloads overlap.
+    const int P = (int)p->rpanels.size(), K = P;
+    const int per = (p->N + K - 1) / K;
+    std::vector<int> need(P);
+    bool banded = true;
+    for (int j = 0; j < P; ++j) {
+      const int cm = p->rpanels[j].col_max;
+      need[j] = cm < 0 ? 0 : std::min(K - 1, cm / per);
+      if (j + 1 < P && need[j] > j + 1) banded = false;
+    }
+    if (banded) {
+      if (!p->down) VCSR_CUDA(cudaStreamCreateWithFlags(&p->down, cudaStreamNonBlocking));
+      if (!p->comp) VCSR_CUDA(cudaStreamCreateWithFlags(&p->comp, cudaStreamNonBlocking));
+      while ((int)p->chunk_done.size() < K + P) {
+        cudaEvent_t e;
+        VCSR_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        p->chunk_done.push_back(e);
+      }
+      const size_t row_b = sizeof(float) * (size_t)O;
+      vcsr_status status = VCSR_OK;
+      cudaError_t e = cudaSuccess;
+      for (int i = 0; i < K && e == cudaSuccess; ++i) {
+        const int r0 = std::min(p->N, i * per), r1 = std::min(p->N, r0 + per);
+        if (r1 > r0)
+          e = cudaMemcpyAsync(p->d_stage_B + (size_t)r0 * O, hB + (size_t)r0 * O,
+                              row_b * (r1 - r0), cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess) e = cudaEventRecord(p->chunk_done[i], st);
+      }
+      if (e != cudaSuccess) status = fail(VCSR_ERR_CUDA, "row upload: %s", cudaGetErrorString(e));
+      for (int j = 0; j < P && status == VCSR_OK; ++j) {
+        const auto &rp = p->rpanels[j];
+        e = cudaStreamWaitEvent(p->comp, p->chunk_done[need[j]], 0);
+        if (e != cudaSuccess) {
+          status = fail(VCSR_ERR_CUDA, "row panel wait: %s", cudaGetErrorString(e));
+          break;
+        }
+        vcsr::PanelDevView v = view(p);
+        v.batches += rp.b0;
+        v.n_batches = rp.b1 - rp.b0;
+        v.long_idx += rp.l0;
+        v.n_long = rp.l1 - rp.l0;
+        status = vcsr::launch_panel_spmm(v, false, p->d_stage_B, O, p->d_stage_C, O, O, p->comp,
+                                         nullptr, p->side, p->fork, p->join);
+        if (status != VCSR_OK) break;
+        e = cudaEventRecord(p->chunk_done[K + j], p->comp);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(p->down, p->chunk_done[K + j], 0);
+        if (e == cudaSuccess && rp.row1 > rp.row0)
+          e = cudaMemcpyAsync(hC + (size_t)rp.row0 * O, p->d_stage_C + (size_t)rp.row0 * O,
+                              row_b * (rp.row1 - rp.row0), cudaMemcpyDeviceToHost, p->down);
+        if (e != cudaSuccess) status = fail(VCSR_ERR_CUDA, "row download: %s", cudaGetErrorString(e));
+      }
+      // every stream drains before returning, also after an error
+      const cudaError_t e1 = cudaStreamSynchronize(p->down), e2 = cudaStreamSynchronize(p->comp),
+                        e3 = cudaStreamSynchronize(st);
+      if (status != VCSR_OK) return status;
+      if (e1 != cudaSuccess || e2 != cudaSuccess || e3 != cudaSuccess)
+        return fail(VCSR_ERR_CUDA, "row pipeline: %s",
+                    cudaGetErrorString(e1 != cudaSuccess ? e1 : (e2 != cudaSuccess ? e2 : e3)));
+      return VCSR_OK;
+    }
+  }
   // Columns of B and C split into chunks are independent products
   // (C[:, chunk] = A * B[:, chunk]).  With large buffers the call runs as a
   // pipeline of up to four chunks: chunk k is uploaded and multiplied on
@@ -514,7 +628,6 @@ vcsr_status vcsr_spmm_host(vcsr_plan *p, const float *hB, float *hC, int O,
   // (w floats out of every row of O); measured on B200 hosts, rows of at
   // least 256 bytes keep both directions at full speed (128-byte rows lose
   // a third), so a chunk is at least 64 floats wide.
-  constexpr size_t kPipelineBytes = (size_t)8 << 20;
   int W = O;
   if (O >= 128 && nb + nc >= kPipelineBytes) {
     const int nch = std::min(4, O / 64);
