@@ -105,6 +105,23 @@ void vcsr_vcsr_free(vcsr_vcsr *v, int where);
  * file, a missing size line or a short/garbled data section. */
 vcsr_status vcsr_read_mtx(const char *path, vcsr_coo *out);
 
+/* Options of vcsr_read_mtx_ex. */
+#define VCSR_MTX_BANNER 1 /* read the %%MatrixMarket banner and follow the standard */
+
+/* Matrix Market reader that follows the format's banner (no counterpart in
+ * the reference, whose reader ignores it: include/mmio.hpp:22-45).  Without
+ * VCSR_MTX_BANNER it is vcsr_read_mtx.  With it: the first line must be
+ * "%%MatrixMarket matrix coordinate <field> <symmetry>"; indices are 1-based;
+ * one entry per line; field real/double/integer as values, pattern entries
+ * get 1, complex keeps the real part; symmetry symmetric / skew-symmetric /
+ * hermitian stores one triangle and every off-diagonal entry is followed by
+ * its mirror (negated for skew-symmetric, the real part for hermitian).
+ * Entries keep file order.  Lines are parsed by all host threads.  Errors:
+ * VCSR_ERR_IO (no banner, bad size line, wrong entry count, bad entry or
+ * index out of range), VCSR_ERR_UNSUPPORTED (array format, other objects,
+ * unknown field or symmetry). */
+vcsr_status vcsr_read_mtx_ex(const char *path, int flags, vcsr_coo *out);
+
 /* COO -> CSR; replaces coo_to_csr (include/csr.hpp:16-37).  Rows are placed by
  * a stable counting sort, then each row's entries are ordered by column; equal
  * columns keep input order.  A row index outside [0,M) is VCSR_ERR_RANGE like

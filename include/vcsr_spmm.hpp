@@ -55,10 +55,12 @@ struct VCSRSpMM {
   std::vector<float> val;
 };
 
-// read_matrix_market_coo (include/mmio.hpp:22-45)
-inline COO read_matrix_market_coo(const std::string &path) {
+// read_matrix_market_coo (include/mmio.hpp:22-45); banner = true follows the
+// %%MatrixMarket banner (pattern, symmetric expansion: vcsr_read_mtx_ex)
+inline COO read_matrix_market_coo(const std::string &path, bool banner = false) {
   vcsr_coo c{};
-  vcsr_detail::check(vcsr_read_mtx(path.c_str(), &c));
+  vcsr_detail::check(banner ? vcsr_read_mtx_ex(path.c_str(), VCSR_MTX_BANNER, &c)
+                            : vcsr_read_mtx(path.c_str(), &c));
   COO o;
   o.M = c.M; o.N = c.N;
   o.rows = vcsr_detail::take(c.rows, (size_t)c.nnz);

@@ -32,7 +32,7 @@ void usage() {
   printf("Usage: spmm_vcsr (--mtx file.mtx | --gen uniform|fem|powerlaw|rmat|blockdense)"
          " --O 128 [options]\n");
   printf("Options: --segw w --bundle b --tileK t --repeat r --algo a --size s --seed s"
-         " --gpus n --check\n");
+         " --gpus n --check --mtx-banner\n");
   printf("Algorithms: cusparse, csr, vcsr, vcsr_seg, vcsr_baseline, aspt, all\n");
 }
 
@@ -76,6 +76,7 @@ double rel_l2(const std::vector<float> &x, const std::vector<float> &r) {
 
 int main(int argc, char **argv) {
   std::string mtx, gen, algo = "all";
+  bool mtx_banner = false;  // follow the %%MatrixMarket banner (symmetric expansion)
   int O = 128, segw = 16, bundle = 32, tileK = 64, repeat = 10, size = 0, gpus = 1;
   unsigned long long seed = 0;
   bool check = false;
@@ -86,11 +87,13 @@ int main(int argc, char **argv) {
       {"algo", required_argument, 0, 'a'},  {"gen", required_argument, 0, 'g'},
       {"size", required_argument, 0, 'z'},  {"seed", required_argument, 0, 'e'},
       {"gpus", required_argument, 0, 'n'},  {"check", no_argument, 0, 'c'},
-      {"help", no_argument, 0, 'h'},        {0, 0, 0, 0}};
+      {"help", no_argument, 0, 'h'},        {"mtx-banner", no_argument, 0, 'x'},
+      {0, 0, 0, 0}};
   int c, idx;
   while ((c = getopt_long(argc, argv, "", opts, &idx)) != -1) {
     switch (c) {
       case 'm': mtx = optarg; break;
+      case 'x': mtx_banner = true; break;
       case 'o': O = atoi(optarg); break;
       case 's': segw = atoi(optarg); break;
       case 'b': bundle = atoi(optarg); break;
@@ -115,7 +118,7 @@ int main(int argc, char **argv) {
   try {
     if (!mtx.empty()) {
       printf("Loading: %s\n", mtx.c_str());
-      COO coo = read_matrix_market_coo(mtx);
+      COO coo = read_matrix_market_coo(mtx, mtx_banner);
       csr = coo_to_csr(coo);
     } else {
       printf("Generating: %s (size %d, seed %llu)\n", gen.c_str(), size, seed);

@@ -6,6 +6,7 @@
 // rewritten for speed (one buffered read, a multi-threaded per-row sort).
 #include <algorithm>
 #include <cerrno>
+#include <charconv>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -168,6 +169,201 @@ vcsr_status vcsr_read_mtx(const char *path, vcsr_coo *out) {
   }
   out->M = (int)M; out->N = (int)N; out->nnz = (int)Z;
   out->rows = R; out->cols = Cc; out->vals = V;
+  return VCSR_OK;
+}
+
+// --------------------------------------------- MTX reader with the banner
+
+namespace {
+
+struct MtxBanner {
+  bool pattern = false, complex_ = false, integer = false;
+  int symmetry = 0;  // 0 general, 1 symmetric, 2 skew-symmetric, 3 hermitian
+};
+
+bool ieq(const std::string &a, const char *b) {
+  size_t n = strlen(b);
+  if (a.size() != n) return false;
+  for (size_t i = 0; i < n; ++i)
+    if (tolower((unsigned char)a[i]) != b[i]) return false;
+  return true;
+}
+
+// One data line: "r c [v [im]]" -> (r, c, v); false when malformed.
+bool parse_entry(const char *b, const char *e, const MtxBanner &mb, long long &r, long long &c,
+                 double &v) {
+  auto skip = [&](const char *q) {
+    while (q < e && is_space(*q)) ++q;
+    return q;
+  };
+  const char *q = skip(b);
+  auto ri = std::from_chars(q, e, r);
+  if (ri.ec != std::errc() || ri.ptr == q) return false;
+  q = skip(ri.ptr);
+  auto ci = std::from_chars(q, e, c);
+  if (ci.ec != std::errc() || ci.ptr == q) return false;
+  q = skip(ci.ptr);
+  if (mb.pattern) {
+    v = 1.0;
+  } else {
+    if (*q == '+') ++q;  // from_chars takes no leading '+'
+    auto vi = std::from_chars(q, e, v);
+    if (vi.ec != std::errc() || vi.ptr == q) return false;
+    q = vi.ptr;
+    if (mb.complex_) {  // the imaginary part is read and dropped
+      q = skip(q);
+      if (*q == '+') ++q;
+      double im;
+      auto ii = std::from_chars(q, e, im);
+      if (ii.ec != std::errc() || ii.ptr == q) return false;
+      q = ii.ptr;
+    }
+  }
+  return skip(q) == e;
+}
+
+}  // namespace
+
+vcsr_status vcsr_read_mtx_ex(const char *path, int flags, vcsr_coo *out) {
+  vcsr::clear_error();
+  if (!path || !out) return fail(VCSR_ERR_INVALID, "null argument");
+  if (!(flags & VCSR_MTX_BANNER)) return vcsr_read_mtx(path, out);
+  std::memset(out, 0, sizeof *out);
+  FILE *f = fopen(path, "rb");
+  if (!f) return fail(VCSR_ERR_IO, "Failed to open MTX: %s", path);
+  std::string buf;
+  if (fseek(f, 0, SEEK_END) == 0) {
+    long sz = ftell(f);
+    if (sz > 0) buf.resize((size_t)sz);
+    fseek(f, 0, SEEK_SET);
+    if (sz > 0 && fread(&buf[0], 1, (size_t)sz, f) != (size_t)sz) {
+      fclose(f);
+      return fail(VCSR_ERR_IO, "Failed to read MTX: %s", path);
+    }
+  }
+  fclose(f);
+  const char *p = buf.data(), *end = p + buf.size();
+  // banner: %%MatrixMarket matrix coordinate <field> <symmetry>
+  MtxBanner mb;
+  {
+    const char *eol = (const char *)memchr(p, '\n', end - p);
+    if (!eol) eol = end;
+    std::string line(p, eol);
+    char w[5][64] = {{0}};
+    if (line.compare(0, 14, "%%MatrixMarket") != 0 ||
+        sscanf(line.c_str(), "%63s %63s %63s %63s %63s", w[0], w[1], w[2], w[3], w[4]) != 5)
+      return fail(VCSR_ERR_IO, "missing %%%%MatrixMarket banner");
+    if (!ieq(w[1], "matrix")) return fail(VCSR_ERR_UNSUPPORTED, "MTX object '%s'", w[1]);
+    if (!ieq(w[2], "coordinate"))
+      return fail(VCSR_ERR_UNSUPPORTED, "MTX format '%s' (only coordinate)", w[2]);
+    const std::string field = w[3], sym = w[4];
+    if (ieq(field, "pattern")) mb.pattern = true;
+    else if (ieq(field, "complex")) mb.complex_ = true;
+    else if (ieq(field, "integer")) mb.integer = true;
+    else if (!ieq(field, "real") && !ieq(field, "double"))
+      return fail(VCSR_ERR_UNSUPPORTED, "MTX field '%s'", w[3]);
+    if (ieq(sym, "general")) mb.symmetry = 0;
+    else if (ieq(sym, "symmetric")) mb.symmetry = 1;
+    else if (ieq(sym, "skew-symmetric")) mb.symmetry = 2;
+    else if (ieq(sym, "hermitian")) mb.symmetry = 3;
+    else return fail(VCSR_ERR_UNSUPPORTED, "MTX symmetry '%s'", w[4]);
+    p = eol < end ? eol + 1 : end;
+  }
+  // size line: first line that is neither empty nor a comment
+  long long M = -1, N = -1, Z = -1;
+  bool found = false;
+  while (p < end) {
+    const char *eol = (const char *)memchr(p, '\n', end - p);
+    if (!eol) eol = end;
+    const char *q = p;
+    while (q < eol && is_space(*q)) ++q;
+    if (q < eol && *q != '%') {
+      std::string line(q, eol);
+      if (sscanf(line.c_str(), "%lld %lld %lld", &M, &N, &Z) != 3)
+        return fail(VCSR_ERR_IO, "Invalid MTX size line");
+      p = eol < end ? eol + 1 : end;
+      found = true;
+      break;
+    }
+    p = eol < end ? eol + 1 : end;
+  }
+  if (!found || M < 0 || N < 0 || Z < 0) return fail(VCSR_ERR_IO, "Invalid MTX size line");
+  if (M > INT32_MAX || N > INT32_MAX || Z > INT32_MAX)
+    return fail(VCSR_ERR_UNSUPPORTED, "MTX dimensions exceed 32-bit indexing");
+  if (mb.symmetry && M != N) return fail(VCSR_ERR_IO, "symmetric MTX must be square");
+  // data lines (one entry per line, blank and '%' lines skipped), parsed in
+  // parallel chunks; each entry is followed by its mirror when the banner
+  // says the file holds one triangle
+  std::vector<const char *> ls;  // starts of non-empty, non-comment lines
+  ls.reserve((size_t)Z + 1);
+  while (p < end) {
+    const char *eol = (const char *)memchr(p, '\n', end - p);
+    if (!eol) eol = end;
+    const char *q = p;
+    while (q < eol && is_space(*q)) ++q;
+    if (q < eol && *q != '%') ls.push_back(p);
+    p = eol < end ? eol + 1 : end;
+  }
+  if ((long long)ls.size() != Z)
+    return fail(VCSR_ERR_IO, "MTX has %zu entries, size line says %lld", ls.size(), Z);
+  const int T = std::max(1, std::min(omp_get_max_threads(), (int)(Z / 65536) + 1));
+  std::vector<long long> cnt(T + 1, 0);
+  std::vector<int> bad(T, 0);
+  std::vector<unsigned char> mirror((size_t)Z, 0);
+  std::vector<int> rr((size_t)Z), cc((size_t)Z);
+  std::vector<float> vv((size_t)Z);
+#pragma omp parallel num_threads(T)
+  {
+    const int t = omp_get_thread_num();
+    const long long i0 = Z * t / T, i1 = Z * (t + 1) / T;
+    long long extra = 0;
+    for (long long i = i0; i < i1; ++i) {
+      const char *b = ls[(size_t)i];
+      const char *eol = (const char *)memchr(b, '\n', end - b);
+      if (!eol) eol = end;
+      long long r, c;
+      double v;
+      if (!parse_entry(b, eol, mb, r, c, v) || r < 1 || c < 1 || r > M || c > N) {
+        bad[t] = 1;
+        break;
+      }
+      rr[(size_t)i] = (int)(r - 1);
+      cc[(size_t)i] = (int)(c - 1);
+      vv[(size_t)i] = (float)v;
+      if (mb.symmetry && r != c) {
+        mirror[(size_t)i] = 1;
+        ++extra;
+      }
+    }
+    cnt[t + 1] = (i1 - i0) + extra;
+  }
+  for (int t = 0; t < T; ++t)
+    if (bad[t]) return fail(VCSR_ERR_IO, "Bad MTX data");
+  for (int t = 0; t < T; ++t) cnt[t + 1] += cnt[t];
+  const long long total = cnt[T];
+  if (total > INT32_MAX) return fail(VCSR_ERR_UNSUPPORTED, "expanded nnz exceeds 32 bits");
+  int *R = (int *)malloc(sizeof(int) * (size_t)(total ? total : 1));
+  int *C = (int *)malloc(sizeof(int) * (size_t)(total ? total : 1));
+  float *V = (float *)malloc(sizeof(float) * (size_t)(total ? total : 1));
+  if (!R || !C || !V) {
+    free(R); free(C); free(V);
+    return fail(VCSR_ERR_ALLOC, "out of host memory");
+  }
+  const float sign = mb.symmetry == 2 ? -1.f : 1.f;
+#pragma omp parallel num_threads(T)
+  {
+    const int t = omp_get_thread_num();
+    const long long i0 = Z * t / T, i1 = Z * (t + 1) / T;
+    long long o = cnt[t];
+    for (long long i = i0; i < i1; ++i) {
+      R[o] = rr[(size_t)i]; C[o] = cc[(size_t)i]; V[o] = vv[(size_t)i]; ++o;
+      if (mirror[(size_t)i]) {
+        R[o] = cc[(size_t)i]; C[o] = rr[(size_t)i]; V[o] = sign * vv[(size_t)i]; ++o;
+      }
+    }
+  }
+  out->M = (int)M; out->N = (int)N; out->nnz = (int)total;
+  out->rows = R; out->cols = C; out->vals = V;
   return VCSR_OK;
 }
 

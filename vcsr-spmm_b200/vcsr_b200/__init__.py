@@ -37,6 +37,7 @@ STATUS = {0: "ok", 1: "invalid", 2: "cuda", 3: "alloc", 4: "io",
 HOST, DEVICE = 0, 1
 PLAN_REFERENCE_FORMAT = 1
 PLAN_TF32_PANELS = 2
+MTX_BANNER = 1
 
 
 class VcsrError(RuntimeError):
@@ -93,6 +94,7 @@ _SIGS = {
     "vcsr_csr_free": (None, [C.POINTER(_Csr), C.c_int]),
     "vcsr_vcsr_free": (None, [C.POINTER(_Vcsr), C.c_int]),
     "vcsr_read_mtx": (C.c_int, [C.c_char_p, C.POINTER(_Coo)]),
+    "vcsr_read_mtx_ex": (C.c_int, [C.c_char_p, C.c_int, C.POINTER(_Coo)]),
     "vcsr_coo_to_csr": (C.c_int, [C.POINTER(_Coo), C.POINTER(_Csr)]),
     "vcsr_gen_csr": (C.c_int, [C.c_char_p, C.c_uint64, C.c_int, C.POINTER(_Csr)]),
     "vcsr_gen_dense": (C.c_int, [C.c_void_p, C.c_int64, C.c_int64, C.c_int64,
@@ -278,11 +280,16 @@ def _vcsr_from_host_struct(v):
     return out
 
 
-def read_matrix_market_coo(path) -> COO:
-    """read_matrix_market_coo (include/mmio.hpp:22-45)."""
+def read_matrix_market_coo(path, banner=False) -> COO:
+    """read_matrix_market_coo (include/mmio.hpp:22-45); with banner=True the
+    Matrix Market banner is followed (pattern / complex fields, symmetric,
+    skew-symmetric and hermitian expansion: vcsr_read_mtx_ex)."""
     L = lib()
     s = _Coo()
-    _check(L.vcsr_read_mtx(os.fsencode(path), C.byref(s)))
+    if banner:
+        _check(L.vcsr_read_mtx_ex(os.fsencode(path), MTX_BANNER, C.byref(s)))
+    else:
+        _check(L.vcsr_read_mtx(os.fsencode(path), C.byref(s)))
     out = COO(s.M, s.N, _take(s.rows, s.nnz, np.int32),
               _take(s.cols, s.nnz, np.int32), _take(s.vals, s.nnz, np.float32))
     L.vcsr_coo_free(C.byref(s))
