@@ -220,6 +220,17 @@ vcsr_status vcsr_plan_get_info(const vcsr_plan *plan, vcsr_plan_info *info);
 vcsr_status vcsr_plan_export(const vcsr_plan *plan, vcsr_vcsr *host_out);
 void vcsr_plan_destroy(vcsr_plan *plan);
 
+/* Plans on disk, so that a matrix's layout is built once.  vcsr_plan_save
+ * writes every array the plan holds (and the segment-major VCSR when the plan
+ * keeps it) with a checksum; vcsr_plan_load reads such a file onto the
+ * current device, on `stream`.  The load checks the checksum, the sizes and
+ * every index the kernels follow before it allocates anything on the device:
+ * VCSR_ERR_IO for a missing, damaged or inconsistent file,
+ * VCSR_ERR_UNSUPPORTED for another file version.  The reference rebuilds its
+ * format on every run (src/main.cpp:113-118); no counterpart there. */
+vcsr_status vcsr_plan_save(const vcsr_plan *plan, const char *path);
+vcsr_status vcsr_plan_load(const char *path, vcsr_plan **out, vcsr_stream_t stream);
+
 /* C = A * B (C written, not accumulated: beta = 0 semantics, the zeroing the
  * reference does with cudaMemset is fused).  B is N x O with leading dimension
  * ldb >= O, C is M x O with ldc >= O, both device pointers.  Replaces the

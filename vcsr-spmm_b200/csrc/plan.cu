@@ -14,76 +14,17 @@
 
 #include "common.h"
 #include "panel.h"
+#include "plan_impl.h"
 #include "panel_tc.h"
 #include "spmm_kernels.h"
 #include "spmm_tc.h"
 
 using vcsr::fail;
+using vcsr::upload;
 
-struct vcsr_plan {
-  int M = 0, N = 0, nnz = 0;
-  vcsr_plan_params params{};
-  int device = 0;
-  // vector panels on the device
-  int R = 1;
-  int num_vectors = 0;
-  int64_t num_union = 0;
-  int chunk = 0;
-  int n_units = 0, n_split_units = 0, n_split_vectors = 0;
-  int *d_ucol = nullptr;
-  float *d_uval = nullptr;
-  int4 *d_units = nullptr;
-  int4 *d_batches = nullptr;
-  int *d_long = nullptr, *d_vec_ptr = nullptr;
-  int n_batches = 0, n_long = 0;
-  int2 *d_parts = nullptr;
-  int2 *d_svecs = nullptr;
-  float *d_partials = nullptr;
-  int *d_counters = nullptr;
-  int pstride = 0, counter_stride = 0;
-  int64_t panel_bytes = 0;
-  // optional segment-major VCSR (include/vcsr.hpp:12-23 layout)
-  bool has_ref = false;
-  vcsr_vcsr ref{};
-  // dense 16x16 panels on the tcgen05 TF32 path (VCSR_PLAN_TF32_PANELS)
-  int *d_rb_row = nullptr, *d_rb_ptr = nullptr, *d_blk_col = nullptr, *d_err = nullptr;
-  float *d_blk_val = nullptr;
-  int n_panel_rb = 0, n_panel_blocks = 0;
-  int64_t panel_nnz = 0;
-  // side stream and events for running long units beside short ones
-  cudaStream_t side = nullptr;
-  cudaEvent_t fork = nullptr, join = nullptr;
-  // host-buffer entry point: staging buffers, the download stream and one
-  // event per column chunk
-  float *d_stage_B = nullptr, *d_stage_C = nullptr;
-  cudaStream_t down = nullptr, comp = nullptr;
-  std::vector<cudaEvent_t> chunk_done;
-  // row panels for the host entry point's row pipeline: vectors
-  // [v0, v1) = batches [b0, b1) + long units [l0, l1); the panel's rows read
-  // B rows up to col_max
-  struct RowPanel {
-    int row0, row1, b0, b1, l0, l1, col_max;
-  };
-  std::vector<RowPanel> rpanels;
-  size_t stage_B = 0, stage_C = 0;
-  double build_ms = 0;
-};
+namespace vcsr {
 
-namespace {
-
-template <class T>
-vcsr_status upload(T **dst, const std::vector<T> &src, cudaStream_t st,
-                   int64_t *bytes) {
-  const size_t n = src.size() ? src.size() : 1;
-  VCSR_CUDA(cudaMalloc((void **)dst, sizeof(T) * n));
-  if (!src.empty())
-    VCSR_CUDA(cudaMemcpyAsync(*dst, src.data(), sizeof(T) * src.size(),
-                              cudaMemcpyHostToDevice, st));
-  if (bytes) *bytes += (int64_t)(sizeof(T) * n);
-  return VCSR_OK;
-}
-
-void release(vcsr_plan *p) {
+void plan_release(vcsr_plan *p) {
   cudaFree(p->d_ucol); cudaFree(p->d_uval); cudaFree(p->d_units);
   cudaFree(p->d_batches); cudaFree(p->d_long); cudaFree(p->d_vec_ptr);
   cudaFree(p->d_parts); cudaFree(p->d_svecs); cudaFree(p->d_partials);
@@ -98,6 +39,29 @@ void release(vcsr_plan *p) {
   if (p->fork) cudaEventDestroy(p->fork);
   if (p->join) cudaEventDestroy(p->join);
 }
+
+vcsr_status plan_finish(vcsr_plan *p, cudaStream_t st) {
+  if (p->n_long > 0 && p->n_batches > 0) {
+    cudaError_t e = cudaStreamCreateWithFlags(&p->side, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->fork, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->join, cudaEventDisableTiming);
+    if (e != cudaSuccess) return fail(VCSR_ERR_CUDA, "side stream: %s", cudaGetErrorString(e));
+  }
+  if (p->n_split_units > 0) {
+    const size_t pbytes = sizeof(float) * (size_t)p->n_split_units * p->R * p->pstride;
+    const size_t cbytes = sizeof(int) * (size_t)p->n_split_vectors * p->counter_stride;
+    cudaError_t e = cudaMalloc(&p->d_partials, pbytes);
+    if (e == cudaSuccess) e = cudaMalloc(&p->d_counters, cbytes);
+    if (e == cudaSuccess) e = cudaMemsetAsync(p->d_counters, 0, cbytes, st);
+    if (e != cudaSuccess) return fail(VCSR_ERR_CUDA, "split scratch: %s", cudaGetErrorString(e));
+    p->panel_bytes += (int64_t)(pbytes + cbytes);
+  }
+  return VCSR_OK;
+}
+
+}  // namespace vcsr
+
+namespace {
 
 vcsr::PanelDevView view(const vcsr_plan *p) {
   vcsr::PanelDevView v;
@@ -391,7 +355,7 @@ vcsr_status vcsr_plan_create(const vcsr_csr *csr, int csr_where,
       (s = upload(&p->d_long, long_idx, st, &p->panel_bytes)) ||
       (s = upload(&p->d_vec_ptr, ph.vec_ptr, st, &p->panel_bytes))) {
     if (owned) vcsr_csr_free(&h, VCSR_HOST);
-    release(p);
+    vcsr::plan_release(p);
     delete p;
     return s;
   }
@@ -403,35 +367,16 @@ vcsr_status vcsr_plan_create(const vcsr_csr *csr, int csr_where,
         (s = upload(&p->d_blk_val, tc.blk_val, st, &p->panel_bytes)) ||
         (s = upload(&p->d_err, zero1, st, &p->panel_bytes))) {
       if (owned) vcsr_csr_free(&h, VCSR_HOST);
-      release(p);
+      vcsr::plan_release(p);
       delete p;
       return s;
     }
   }
-  if (p->n_long > 0 && p->n_batches > 0) {
-    cudaError_t e = cudaStreamCreateWithFlags(&p->side, cudaStreamNonBlocking);
-    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->fork, cudaEventDisableTiming);
-    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->join, cudaEventDisableTiming);
-    if (e != cudaSuccess) {
-      if (owned) vcsr_csr_free(&h, VCSR_HOST);
-      release(p);
-      delete p;
-      return fail(VCSR_ERR_CUDA, "side stream: %s", cudaGetErrorString(e));
-    }
-  }
-  if (p->n_split_units > 0) {
-    const size_t pbytes = sizeof(float) * (size_t)p->n_split_units * p->R * p->pstride;
-    const size_t cbytes = sizeof(int) * (size_t)p->n_split_vectors * p->counter_stride;
-    cudaError_t e = cudaMalloc(&p->d_partials, pbytes);
-    if (e == cudaSuccess) e = cudaMalloc(&p->d_counters, cbytes);
-    if (e == cudaSuccess) e = cudaMemsetAsync(p->d_counters, 0, cbytes, st);
-    if (e != cudaSuccess) {
-      if (owned) vcsr_csr_free(&h, VCSR_HOST);
-      release(p);
-      delete p;
-      return fail(VCSR_ERR_CUDA, "split scratch: %s", cudaGetErrorString(e));
-    }
-    p->panel_bytes += (int64_t)(pbytes + cbytes);
+  if ((s = vcsr::plan_finish(p, st)) != VCSR_OK) {
+    if (owned) vcsr_csr_free(&h, VCSR_HOST);
+    vcsr::plan_release(p);
+    delete p;
+    return s;
   }
   if (params->flags & VCSR_PLAN_REFERENCE_FORMAT) {
     vcsr_csr d{};
@@ -443,7 +388,7 @@ vcsr_status vcsr_plan_create(const vcsr_csr *csr, int csr_where,
     }
     if (s != VCSR_OK) {
       if (owned) vcsr_csr_free(&h, VCSR_HOST);
-      release(p);
+      vcsr::plan_release(p);
       delete p;
       return s;
     }
@@ -452,7 +397,7 @@ vcsr_status vcsr_plan_create(const vcsr_csr *csr, int csr_where,
   cudaError_t e = cudaStreamSynchronize(st);  // host vectors die here
   if (owned) vcsr_csr_free(&h, VCSR_HOST);
   if (e != cudaSuccess) {
-    release(p);
+    vcsr::plan_release(p);
     delete p;
     return fail(VCSR_ERR_CUDA, "plan upload: %s", cudaGetErrorString(e));
   }
@@ -493,7 +438,7 @@ vcsr_status vcsr_plan_export(const vcsr_plan *p, vcsr_vcsr *host_out) {
 
 void vcsr_plan_destroy(vcsr_plan *p) {
   if (!p) return;
-  release(p);
+  vcsr::plan_release(p);
   delete p;
 }
 

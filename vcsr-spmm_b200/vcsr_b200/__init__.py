@@ -115,6 +115,8 @@ _SIGS = {
     "vcsr_spmm_host": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
                                  C.c_void_p]),
     "vcsr_plan_check": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "vcsr_plan_save": (C.c_int, [C.c_void_p, C.c_char_p]),
+    "vcsr_plan_load": (C.c_int, [C.c_char_p, C.POINTER(C.c_void_p), C.c_void_p]),
     "vcsr_spmm_segmented": (C.c_int, [C.POINTER(_Vcsr), C.c_void_p, C.c_int, C.c_int,
                                       C.c_void_p, C.c_void_p]),
     "vcsr_csr_spmm": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
@@ -490,6 +492,22 @@ class Plan:
                                _stream(stream), C.byref(n)))
         self.last_launches = n.value
         return Cout
+
+    def save(self, path):
+        """Write the plan to `path` (vcsr_plan_save)."""
+        _check(lib().vcsr_plan_save(self._h, os.fsencode(path)))
+
+    @classmethod
+    def load(cls, path, stream=None):
+        """A plan read from a file written by save() (vcsr_plan_load)."""
+        h = C.c_void_p()
+        _check(lib().vcsr_plan_load(os.fsencode(path), C.byref(h), _stream(stream)))
+        self = cls.__new__(cls)
+        self._h = h
+        i = self.info()
+        self.M, self.N, self.nnz = i["M"], i["N"], i["nnz"]
+        self.last_launches = 0
+        return self
 
     def check(self, stream=None):
         """Synchronise and raise VcsrError (status 7) if a bounded wait of the
