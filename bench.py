@@ -179,7 +179,12 @@ def cpu_reference(csr, B, seconds, min_reps=3):
     """The reference CSR algorithm on all host cores (oracle port)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
-    threads = oracle.max_threads()
+    # every core this process may run on: torchrun sets OMP_NUM_THREADS=1 for
+    # its ranks, which must not shrink the CPU arm
+    try:
+        threads = len(os.sched_getaffinity(0))
+    except AttributeError:
+        threads = os.cpu_count() or oracle.max_threads()
     M = csr.M
     flops_full = 2.0 * csr.nnz * B.shape[1]
     # bounded sample: leading rows holding at most ~2 GFLOP per repetition
