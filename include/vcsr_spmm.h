@@ -326,6 +326,11 @@ void vcsr_cusparse_destroy(vcsr_cusparse *h);
  * align (rows), kept non-decreasing.  Host-only. */
 vcsr_status vcsr_partition_rows(const int *row_ptr, int M, int parts,
                                 int align, int *cuts);
+/* The same with a per-row cost: row r weighs (its nnz + row_weight), so
+ * panels of many short rows get fewer rows (each row also costs a C row write
+ * and its own setup).  row_weight = 0 is vcsr_partition_rows. */
+vcsr_status vcsr_partition_rows_weighted(const int *row_ptr, int M, int parts, int align,
+                                         double row_weight, int *cuts);
 
 /* Extract rows [r0, r1) of a host CSR as a new host CSR (row ids local). */
 vcsr_status vcsr_csr_row_panel(const vcsr_csr *csr, int r0, int r1,

@@ -167,6 +167,21 @@ def test_partition_rows_balanced():
         assert all(c % 32 == 0 for c in cuts[:-1])
         nnz = np.diff(f.row_ptr[cuts])
         assert nnz.max() - nnz.min() <= 2 * 32 * 80  # within an align window
+    # weighted cuts: row r weighs nnz_r + w; w = 0 is the unweighted cut, and a
+    # matrix whose first half has long rows gets more of its short rows per
+    # panel as w grows
+    rp = np.concatenate([[0], np.cumsum(np.r_[np.full(1000, 40), np.full(3000, 2)])]).astype(np.int32)
+    assert np.array_equal(V.partition_rows(rp, 4, 8, 0.0), V.partition_rows(rp, 4, 8))
+    prev = None
+    for w in (0.0, 2.0, 10.0, 100.0):
+        cuts = V.partition_rows(rp, 2, 8, w)
+        cost = np.diff(rp[cuts]) + w * np.diff(cuts)
+        assert abs(cost[0] - cost[1]) <= 8 * (40 + w) + 1
+        if prev is not None:
+            assert cuts[1] >= prev
+        prev = cuts[1]
+    with pytest.raises(V.VcsrError):
+        V.partition_rows(rp, 2, 8, -1.0)
     p = V.csr_row_panel(f, 100, 200)
     assert p.M == 100 and p.N == f.N
     assert np.array_equal(p.col, f.col[f.row_ptr[100]:f.row_ptr[200]])

@@ -435,23 +435,24 @@ vcsr_status vcsr_coo_to_csr(const vcsr_coo *coo, vcsr_csr *out) {
 
 // ------------------------------------------------------- partitioning
 
-vcsr_status vcsr_partition_rows(const int *row_ptr, int M, int parts, int align,
-                                int *cuts) {
+vcsr_status vcsr_partition_rows_weighted(const int *row_ptr, int M, int parts, int align,
+                                         double row_weight, int *cuts) {
   vcsr::clear_error();
-  if (!row_ptr || !cuts || M < 0 || parts <= 0 || align <= 0)
+  if (!row_ptr || !cuts || M < 0 || parts <= 0 || align <= 0 || !(row_weight >= 0))
     return fail(VCSR_ERR_INVALID, "bad partition arguments");
-  const int64_t nnz = row_ptr[M];
+  // cost of rows [0, r): row_ptr[r] + row_weight * r, non-decreasing in r
+  auto cost = [&](int r) { return (double)row_ptr[r] + row_weight * r; };
+  const double total = cost(M);
   cuts[0] = 0;
   for (int k = 1; k < parts; ++k) {
-    const int64_t target = (nnz * k + parts / 2) / parts;
-    // first row r with row_ptr[r] >= target
-    int lo = 0, hi = M;
+    const double target = total * k / parts;
+    int lo = 0, hi = M;  // first row r with cost(r) >= target
     while (lo < hi) {
       int mid = lo + (hi - lo) / 2;
-      if (row_ptr[mid] < target) lo = mid + 1; else hi = mid;
+      if (cost(mid) < target) lo = mid + 1; else hi = mid;
     }
     int r = lo;
-    if (r > 0 && target - row_ptr[r - 1] < row_ptr[r] - target) r = r - 1;
+    if (r > 0 && target - cost(r - 1) < cost(r) - target) r = r - 1;
     int64_t ra = ((int64_t)r + align / 2) / align * align;
     if (ra > M) ra = M;
     if (ra < cuts[k - 1]) ra = cuts[k - 1];
@@ -459,6 +460,11 @@ vcsr_status vcsr_partition_rows(const int *row_ptr, int M, int parts, int align,
   }
   cuts[parts] = M;
   return VCSR_OK;
+}
+
+vcsr_status vcsr_partition_rows(const int *row_ptr, int M, int parts, int align,
+                                int *cuts) {
+  return vcsr_partition_rows_weighted(row_ptr, M, parts, align, 0.0, cuts);
 }
 
 vcsr_status vcsr_csr_row_panel(const vcsr_csr *csr, int r0, int r1,

@@ -130,6 +130,8 @@ _SIGS = {
     "vcsr_cusparse_run": (C.c_int, [C.c_void_p, C.c_void_p]),
     "vcsr_cusparse_destroy": (None, [C.c_void_p]),
     "vcsr_partition_rows": (C.c_int, [_i32p, C.c_int, C.c_int, C.c_int, _i32p]),
+    "vcsr_partition_rows_weighted": (C.c_int, [_i32p, C.c_int, C.c_int, C.c_int, C.c_double,
+                                               _i32p]),
     "vcsr_csr_row_panel": (C.c_int, [C.POINTER(_Csr), C.c_int, C.c_int,
                                      C.POINTER(_Csr)]),
     "vcsr_mgpu_create": (C.c_int, [C.POINTER(_Csr), C.c_int, _i32p,
@@ -333,11 +335,13 @@ def gen_dense_device(t, seed, lo=-1.0, hi=1.0, stream=None):
     return t
 
 
-def partition_rows(row_ptr, parts, align=1) -> np.ndarray:
+def partition_rows(row_ptr, parts, align=1, row_weight=0.0) -> np.ndarray:
+    """Row cuts of balanced panels: each row weighs its nnz + row_weight."""
     rp = np.ascontiguousarray(row_ptr, np.int32)
     cuts = np.zeros(parts + 1, np.int32)
-    _check(lib().vcsr_partition_rows(rp.ctypes.data_as(_i32p), len(rp) - 1, parts,
-                                     align, cuts.ctypes.data_as(_i32p)))
+    _check(lib().vcsr_partition_rows_weighted(rp.ctypes.data_as(_i32p), len(rp) - 1, parts,
+                                              align, float(row_weight),
+                                              cuts.ctypes.data_as(_i32p)))
     return cuts
 
 
