@@ -28,6 +28,8 @@
 #include <cuda_runtime.h>
 
 #include <mutex>
+#include <utility>
+#include <vector>
 
 #include "common.h"
 #include "spmm_kernels.h"
@@ -559,9 +561,14 @@ __global__ void __launch_bounds__(256, (min_blocks_for<R, NV, VW>()))
     BatchCursor bc{0, 0, 0, nullptr};
     if constexpr (kBatch) {
       const int4 bt = __ldg(P.batches + s);  // {v0, v1, first column, end column}
-      for (int i = sl; i <= bt.y - bt.x; i += L) svp[i] = __ldg(P.vec_ptr + bt.x + i);
-      __syncwarp(submask);
-      bc = BatchCursor{bt.x, svp[1], bt.x, svp};
+      if (bt.y - bt.x == 1) {
+        // one vector: it ends where the batch ends, no boundaries to stage
+        bc = BatchCursor{bt.x, bt.w, bt.x, svp};
+      } else {
+        for (int i = sl; i <= bt.y - bt.x; i += L) svp[i] = __ldg(P.vec_ptr + bt.x + i);
+        __syncwarp(submask);
+        bc = BatchCursor{bt.x, svp[1], bt.x, svp};
+      }
       walk_unit<R, NV, VW, true>(P, B, ldb, bt.z, bt.w, kk, ok, 0, 1, sl, L, submask, L,
                                  chunk, bcol, bval, acc, bc, bt.y, C, ldc);
       __syncwarp(submask);  // svp is rewritten by the next batch
@@ -699,16 +706,49 @@ int stage_chunk_cols(int R, int G) {
 
 namespace {
 
+// Resident CTAs per SM of (kernel, dynamic shared memory, device), asked of
+// the runtime once: the query (and the shared-memory attribute) cost host time
+// that a small launch would otherwise wait for on the GPU.
+vcsr_status resident_per_sm(KernelFn fn, int threads, size_t smem, int *per_sm) {
+  struct Key {
+    KernelFn fn;
+    size_t smem;
+    int dev;
+  };
+  static std::vector<std::pair<Key, int>> cache;
+  static std::mutex mu;
+  int dev = 0;
+  VCSR_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(mu);
+  for (const auto &e : cache)
+    if (e.first.fn == fn && e.first.smem == smem && e.first.dev == dev) {
+      *per_sm = e.second;
+      return VCSR_OK;
+    }
+  // the kernel's dynamic shared-memory limit is raised once, to the device's
+  // opt-in maximum (it only bounds what a launch may ask for), so that no
+  // launch ever lowers it under the size of another
+  bool raised = false;
+  for (const auto &e : cache) raised = raised || (e.first.fn == fn && e.first.dev == dev);
+  if (!raised) {
+    int optin = 0;
+    VCSR_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+    VCSR_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, optin));
+  }
+  int n = 0;
+  VCSR_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, threads, smem));
+  if (n <= 0) n = 1;
+  cache.push_back({Key{fn, smem, dev}, n});
+  *per_sm = n;
+  return VCSR_OK;
+}
+
 vcsr_status launch_one(KernelFn fn, const PanelDevView &P, long long team_items, int G,
                        const LaunchShape &s, int chunk, size_t smem, const float *B, int ldb,
                        float *C, int ldc, int O, cudaStream_t st) {
   const int threads = 256;
-  if (smem > 48 * 1024)
-    VCSR_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)smem));
   int per_sm = 0;
-  VCSR_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem));
-  if (per_sm <= 0) per_sm = 1;
+  VCSR_TRY(resident_per_sm(fn, threads, smem, &per_sm));
   const long long items = team_items * s.n_otiles;
   long long blocks = (items + (threads / 32) - 1) / (threads / 32);
   const long long cap = (long long)sm_count() * per_sm;
