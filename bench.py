@@ -15,6 +15,8 @@ Workloads (synthetic stand-ins with the benchmark configurations' shapes):
   blockdense (O=512): single-panel variants (weak scaling under N GPUs).
   blockdense_tf32  the same matrix with its dense 16x16 blocks on the
                  tensor cores in TF32 (VCSR_PLAN_TF32_PANELS).
+  rmat_bf16, fem_bf16  B held in bfloat16, widened to FP32 on load
+                 (vcsr_spmm_bf16): half the B bytes, FP32 sums.
   rmat           2^22 R-MAT, O = 256: A cut into N nnz-balanced row panels,
                  B broadcast once: strong scaling.
 
@@ -48,9 +50,13 @@ WORKLOADS = {
     "blockdense": ("blockdense", 0, 512, "weak", "blockdense_65536_O512_fp32"),
     "blockdense_tf32": ("blockdense", 0, 512, "weak", "blockdense_65536_O512_tf32"),
     "rmat": ("rmat", 22, 256, "strong", "rmat_s22_O256"),
+    "rmat_bf16": ("rmat", 22, 256, "strong", "rmat_s22_O256_bf16in"),
+    "fem_bf16": ("fem", 0, 128, "weak", "fem_banded_62451_O128_bf16in"),
 }
 # workloads whose dense 16x16 blocks run on the tcgen05 TF32 path
 TF32_WORKLOADS = {"blockdense_tf32"}
+# workloads whose B is held in bfloat16 (FP32 sums: vcsr_spmm_bf16)
+BF16_WORKLOADS = {"rmat_bf16", "fem_bf16"}
 
 
 def parse():
@@ -170,9 +176,9 @@ sys.stdout.flush()
                 "window_ms": round((self.t1 - self.t0) * 1e3, 3)}
 
 
-def algorithmic_bytes(csr, O):
+def algorithmic_bytes(csr, O, b_bytes=4):
     touched = int(np.count_nonzero(np.bincount(csr.col, minlength=csr.N))) if csr.nnz else 0
-    return 8 * csr.nnz + 4 * (csr.M + 1) + 4 * O * touched + 4 * O * csr.M, touched
+    return (8 * csr.nnz + 4 * (csr.M + 1) + b_bytes * O * touched + 4 * O * csr.M), touched
 
 
 def cpu_reference(csr, B, seconds, min_reps=3):
@@ -280,8 +286,15 @@ def run_ours(args):
     bcast_ms = None
     if rank == 0 or world == 1:
         V.gen_dense_device(dB, args.seed + 1000, lo, 1.0)
+    bf16 = args.workload in BF16_WORKLOADS
+    dB32 = dB  # FP32 copy for the peers and the CPU baseline
+    if bf16:
+        dB32 = dB.to(torch.bfloat16).float()  # the values the BF16 path sees
+        dB = dB.to(torch.bfloat16)
     if world > 1:
         torch.cuda.synchronize()
+        if bf16:
+            D.broadcast_b(dist, dB32, 0)
         D.broadcast_b(dist, dB, 0)  # first collective on this buffer: NCCL set-up
         torch.cuda.synchronize()
         dist.barrier()
@@ -333,7 +346,7 @@ def run_ours(args):
     value = flops_step / (ms_step * 1e-3) / 1e9
 
     # roofline of the dominant (only) kernel, per launch, on this rank
-    abytes, touched = algorithmic_bytes(csr, O)
+    abytes, touched = algorithmic_bytes(csr, O, 2 if bf16 else 4)
     avg_ms = float(np.mean(per))
     achieved = abytes / (avg_ms * 1e-3) / 1e9
     peak, peak_kind = peaks()
@@ -341,9 +354,9 @@ def run_ours(args):
 
     # end to end through the host-buffer entry point (pinned buffers)
     e2e = None
-    if not args.no_e2e:
+    if not args.no_e2e and not bf16:  # the host-buffer entry point takes FP32 B
         hB = torch.empty(csr.N, O, dtype=torch.float32, pin_memory=True)
-        hB.copy_(dB.cpu())
+        hB.copy_(dB32.cpu())
         hC = torch.empty(csr.M, O, dtype=torch.float32, pin_memory=True)
         for _ in range(max(1, min(3, args.warmup))):
             plan.spmm_host(hB.numpy(), hC.numpy(), stream=stream)
@@ -371,7 +384,7 @@ def run_ours(args):
         best = None
         for alg in (0, 1, 2, 3):
             try:
-                h = V.CuSparse(d, dB, O, dCp, alg=alg)
+                h = V.CuSparse(d, dB32, O, dCp, alg=alg)
             except V.VcsrError:
                 continue
             for _ in range(3):
@@ -398,7 +411,7 @@ def run_ours(args):
             flush.zero_()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(stream)
-            V.run_csr_spmm_gpu(csr.M, d.row_ptr, d.col, d.val, dB, O, dCp, stream)
+            V.run_csr_spmm_gpu(csr.M, d.row_ptr, d.col, d.val, dB32, O, dCp, stream)
             b.record(stream)
             torch.cuda.synchronize()
             ts.append(a.elapsed_time(b))
@@ -406,7 +419,7 @@ def run_ours(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        B = dB.cpu().numpy()
+        B = dB32.cpu().numpy()
         cpu = cpu_reference(csr, B, args.cpu_seconds)
 
     if world > 1:
@@ -416,7 +429,7 @@ def run_ours(args):
             "metric": METRIC, "value": round(value, 3), "unit": "GFLOP/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms_step, 5), "higher_is_better": True,
-            "scaling": scaling, "vs_baseline": None, "dtype": "tf32" if tf32 else "f32",
+            "scaling": scaling, "vs_baseline": None, "dtype": "tf32" if tf32 else ("bf16-in/f32-acc" if bf16 else "f32"),
             "data": "synthetic",
             "config": {"workload": label, "M": csr.M, "N": csr.N, "nnz": csr.nnz,
                        "global_nnz": global_nnz, "O": O, "segw": 4, "bundle": 32,

@@ -242,6 +242,17 @@ vcsr_status vcsr_spmm(const vcsr_plan *plan, const float *dB, int ldb,
                       float *dC, int ldc, int O, vcsr_stream_t stream,
                       int *launches);
 
+/* C = A * B with B in BF16 (bfloat16 bits, N x O, leading dimension ldb);
+ * each B value is widened to FP32 as it is loaded (exact) and the sums are the
+ * FP32 path's, so C equals, bit for bit, vcsr_spmm on the widened B.  B traffic
+ * is half of FP32's (gather-bound matrices such as R-MAT gain most).  Not for
+ * plans with TF32 panels (VCSR_ERR_UNSUPPORTED); same other rules as
+ * vcsr_spmm.  The reference's only reduced-precision path is its FP16 WMMA
+ * kernel (src/vcsr_tc.cu); no direct counterpart. */
+vcsr_status vcsr_spmm_bf16(const vcsr_plan *plan, const void *dB, int ldb,
+                           float *dC, int ldc, int O, vcsr_stream_t stream,
+                           int *launches);
+
 /* The same product with host buffers: copies hB (N x O, ld = O) to the device,
  * runs vcsr_spmm, copies C back to hC (M x O, ld = O) and synchronises the
  * stream.  Replaces the upload/launch/download sequence of the reference's

@@ -474,6 +474,25 @@ vcsr_status vcsr_spmm(const vcsr_plan *p, const float *dB, int ldb, float *dC,
   return VCSR_OK;
 }
 
+vcsr_status vcsr_spmm_bf16(const vcsr_plan *p, const void *dB, int ldb, float *dC, int ldc,
+                           int O, vcsr_stream_t stream, int *launches) {
+  vcsr::clear_error();
+  if (launches) *launches = 0;
+  if (!p) return fail(VCSR_ERR_INVALID, "null plan");
+  if (O < 0 || ldb < O || ldc < O)
+    return fail(VCSR_ERR_INVALID, "need 0 <= O <= ldb, ldc (O=%d ldb=%d ldc=%d)", O, ldb, ldc);
+  if (O == 0 || p->M == 0) return VCSR_OK;
+  if (!dC || (!dB && p->N > 0)) return fail(VCSR_ERR_INVALID, "null B or C");
+  if (p->n_panel_rb > 0)
+    return fail(VCSR_ERR_UNSUPPORTED, "a plan with TF32 panels reads B in FP32");
+  if ((uintptr_t)dB % 2) return fail(VCSR_ERR_INVALID, "BF16 B must be 2-byte aligned");
+  if (p->n_split_units > 0 && O > p->pstride)
+    return fail(VCSR_ERR_INVALID,
+                "O=%d exceeds the plan's max_O=%d (split rows need scratch)", O, p->pstride);
+  return vcsr::launch_panel_spmm(view(p), false, dB, ldb, dC, ldc, O, (cudaStream_t)stream,
+                                 launches, p->side, p->fork, p->join, true);
+}
+
 vcsr_status vcsr_spmm_host(vcsr_plan *p, const float *hB, float *hC, int O,
                            vcsr_stream_t stream) {
   vcsr::clear_error();

@@ -42,10 +42,12 @@ LaunchShape pick_shape(int O, int R, bool vec4);
 
 // Launches the long-unit kernel (on `side`, forked from and joined back to
 // `st` with the two events, when there is short work too) and the short-work
-// kernel (on `st`).  side may be null: then both run on `st`.
+// kernel (on `st`).  side may be null: then both run on `st`.  B holds FP32
+// values, or BF16 ones with bf16 = true (widened to FP32 as they are loaded;
+// not for the plain-CSR rowptr form).
 vcsr_status launch_panel_spmm(const PanelDevView &P, bool rowptr,
-                              const float *B, int ldb, float *C, int ldc, int O,
+                              const void *B, int ldb, float *C, int ldc, int O,
                               cudaStream_t st, int *launches, cudaStream_t side,
-                              cudaEvent_t fork, cudaEvent_t join);
+                              cudaEvent_t fork, cudaEvent_t join, bool bf16 = false);
 
 }  // namespace vcsr

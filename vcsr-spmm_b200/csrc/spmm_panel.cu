@@ -27,6 +27,8 @@
 // (beta = 0), with streaming stores.
 #include <cuda_runtime.h>
 
+#include <cuda_bf16.h>
+
 #include <mutex>
 #include <utility>
 #include <vector>
@@ -80,6 +82,30 @@ struct VecT<1> {
   static __device__ __forceinline__ T add(T a, T b) { return a + b; }
   static __device__ __forceinline__ T shfl_xor(unsigned m, T v, int o) {
     return __shfl_xor_sync(m, v, o);
+  }
+};
+
+// B values widened to FP32 as they are loaded: FP32 as stored; BF16 by
+// placing its 16 bits in the high half of a float (exact), four values per
+// 8-byte load with 128-bit lanes.
+template <int VW>
+struct LdB;
+template <>
+struct LdB<4> {
+  static __device__ __forceinline__ float4 ld(const float *p) {
+    return __ldg(reinterpret_cast<const float4 *>(p));
+  }
+  static __device__ __forceinline__ float4 ld(const __nv_bfloat16 *p) {
+    const uint2 u = __ldg(reinterpret_cast<const uint2 *>(p));
+    return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
+                       __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
+  }
+};
+template <>
+struct LdB<1> {
+  static __device__ __forceinline__ float ld(const float *p) { return __ldg(p); }
+  static __device__ __forceinline__ float ld(const __nv_bfloat16 *p) {
+    return __uint_as_float((unsigned)__ldg(reinterpret_cast<const unsigned short *>(p)) << 16);
   }
 };
 
@@ -260,8 +286,8 @@ struct Acc<R, NV, 1> {
 };
 
 // B values of UN columns j0, j0+step, ...; FULL = all UN exist.
-template <int NV, int VW, int UN, bool FULL>
-__device__ __forceinline__ void load_group(const float *__restrict__ Bk, int ldb,
+template <int NV, int VW, int UN, bool FULL, class TB = float>
+__device__ __forceinline__ void load_group(const TB *__restrict__ Bk, int ldb,
                                            const int *scol, int j0, int step, int n,
                                            const bool (&ok)[NV], int vstride,
                                            typename VecT<VW>::T (&b)[UN][NV]) {
@@ -270,9 +296,9 @@ __device__ __forceinline__ void load_group(const float *__restrict__ Bk, int ldb
   for (int q = 0; q < UN; ++q) {
     const int j = j0 + q * step;
     if (FULL || j < n) {
-      const float *bp = Bk + (size_t)scol[j] * ldb;
+      const TB *bp = Bk + (size_t)scol[j] * ldb;
 #pragma unroll
-      for (int v = 0; v < NV; ++v) b[q][v] = ok[v] ? V::ld(bp + v * vstride) : V::zero();
+      for (int v = 0; v < NV; ++v) b[q][v] = ok[v] ? LdB<VW>::ld(bp + v * vstride) : V::zero();
     }
   }
 }
@@ -340,9 +366,9 @@ __device__ __forceinline__ void fma_group(const float *sval, int j0, int step, i
 // are left reduced in `out`.  With BATCH (ncg = 1) they span vectors
 // [bc.v0, v1): each vector's rows are written to C when its last column has
 // been added, the last ones (and trailing empty vectors) at the end.
-template <int R, int NV, int VW, bool BATCH>
+template <int R, int NV, int VW, bool BATCH, class TB = float>
 __device__ __forceinline__ void walk_unit(
-    const PanelDevView &P, const float *__restrict__ B, int ldb, int begin, int end,
+    const PanelDevView &P, const TB *__restrict__ B, int ldb, int begin, int end,
     const int (&kk)[NV], const bool (&ok)[NV], int cg, int ncg, int t, int T,
     unsigned tmask, int L, int chunk, int *buf_col, float *buf_val,
     typename VecT<VW>::T (&out)[R][NV], BatchCursor &bc, int v1,
@@ -352,7 +378,7 @@ __device__ __forceinline__ void walk_unit(
   constexpr int UN = unroll_for<R, NV, VW>();
   Acc<R, NV, VW> acc;
   acc.zero();
-  const float *Bk = B + kk[0];
+  const TB *Bk = B + kk[0];
   const int vstride = L * VW;
   if (begin < end) {
     // prologue: stage chunk 0 into buffer 0
@@ -379,10 +405,10 @@ __device__ __forceinline__ void walk_unit(
       Tv b0[UN][NV], b1[UN][NV];
       int j = cg;
       if (nfull > 0)
-        load_group<NV, VW, UN, true>(Bk, ldb, scol, j, ncg, n, ok, vstride, b0);
+        load_group<NV, VW, UN, true, TB>(Bk, ldb, scol, j, ncg, n, ok, vstride, b0);
       for (int g = 0; g < nfull; g += 2) {
         if (g + 1 < nfull)
-          load_group<NV, VW, UN, true>(Bk, ldb, scol, j + gstep, ncg, n, ok, vstride, b1);
+          load_group<NV, VW, UN, true, TB>(Bk, ldb, scol, j + gstep, ncg, n, ok, vstride, b1);
         fma_group<R, NV, VW, UN, true, BATCH>(sval, j, ncg, n, b0, acc, c0, bc, C, ldc,
                                               P.M, kk, ok);
         if (g + 1 >= nfull) {
@@ -390,14 +416,14 @@ __device__ __forceinline__ void walk_unit(
           break;
         }
         if (g + 2 < nfull)
-          load_group<NV, VW, UN, true>(Bk, ldb, scol, j + 2 * gstep, ncg, n, ok, vstride,
+          load_group<NV, VW, UN, true, TB>(Bk, ldb, scol, j + 2 * gstep, ncg, n, ok, vstride,
                                        b0);
         fma_group<R, NV, VW, UN, true, BATCH>(sval, j + gstep, ncg, n, b1, acc, c0, bc, C,
                                               ldc, P.M, kk, ok);
         j += 2 * gstep;
       }
       if (j < n) {
-        load_group<NV, VW, UN, false>(Bk, ldb, scol, j, ncg, n, ok, vstride, b0);
+        load_group<NV, VW, UN, false, TB>(Bk, ldb, scol, j, ncg, n, ok, vstride, b0);
         fma_group<R, NV, VW, UN, false, BATCH>(sval, j, ncg, n, b0, acc, c0, bc, C, ldc,
                                                P.M, kk, ok);
       }
@@ -521,11 +547,12 @@ constexpr int kBatchVP = 68;    // staged vec_ptr entries per team (>= kBatchVec
 // vectors (for R <= 2 the sub-warp streams through all of them and writes
 // each vector's rows at its boundary; for R >= 4 a batch is one vector).
 // ROWPTR (plain CSR): one row.
-template <int R, int NV, int VW, bool ROWPTR>
+template <int R, int NV, int VW, bool ROWPTR, class TB>
 __global__ void __launch_bounds__(256, (min_blocks_for<R, NV, VW>()))
-    panel_short_kernel(const PanelDevView P, const float *__restrict__ B, int ldb,
+    panel_short_kernel(const PanelDevView P, const void *__restrict__ Bv, int ldb,
                        float *__restrict__ C, int ldc, int O, int lshift, int n_otiles,
                        int W, int chunk) {
+  const TB *B = static_cast<const TB *>(Bv);
   using Tv = typename VecT<VW>::T;
   constexpr bool kBatch = !ROWPTR && R <= 2;
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -589,13 +616,14 @@ __global__ void __launch_bounds__(256, (min_blocks_for<R, NV, VW>()))
 
 // Long work: a whole warp per long unit or split part, its sub-warps taking
 // every G-th union column; split parts finish through the part tickets.
-template <int R, int NV, int VW>
+template <int R, int NV, int VW, class TB>
 __global__ void __launch_bounds__(256, (min_blocks_for<R, NV, VW>() < 2
                                             ? min_blocks_for<R, NV, VW>()
                                             : 2))
-    panel_long_kernel(const PanelDevView P, const float *__restrict__ B, int ldb,
+    panel_long_kernel(const PanelDevView P, const void *__restrict__ Bv, int ldb,
                       float *__restrict__ C, int ldc, int O, int lshift, int n_otiles,
                       int W, int chunk) {
+  const TB *B = static_cast<const TB *>(Bv);
   using Tv = typename VecT<VW>::T;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int L = 1 << lshift;
@@ -628,38 +656,47 @@ __global__ void __launch_bounds__(256, (min_blocks_for<R, NV, VW>() < 2
   }
 }
 
-using KernelFn = void (*)(const PanelDevView, const float *, int, float *, int, int,
+using KernelFn = void (*)(const PanelDevView, const void *, int, float *, int, int,
                           int, int, int, int);
 
-template <int R, int NV, int VW>
+template <int R, int NV, int VW, class TB>
 KernelFn pick_rv(bool is_long, bool rowptr) {
-  if (is_long) return panel_long_kernel<R, NV, VW>;
+  if (is_long) return panel_long_kernel<R, NV, VW, TB>;
   if constexpr (R == 1) {
-    if (rowptr) return panel_short_kernel<1, NV, VW, true>;
+    if (rowptr) {
+      if constexpr (std::is_same<TB, float>::value) return panel_short_kernel<1, NV, VW, true, TB>;
+      return nullptr;  // the plain-CSR entry points take FP32 B only
+    }
   }
-  return panel_short_kernel<R, NV, VW, false>;
+  return panel_short_kernel<R, NV, VW, false, TB>;
 }
 
-template <int R>
+template <int R, class TB>
 KernelFn pick_r(int NV, int VW, bool is_long, bool rowptr) {
   if constexpr (R == 16) {
-    return VW == 4 ? pick_rv<16, 1, 4>(is_long, rowptr) : pick_rv<16, 1, 1>(is_long, rowptr);
+    return VW == 4 ? pick_rv<16, 1, 4, TB>(is_long, rowptr) : pick_rv<16, 1, 1, TB>(is_long, rowptr);
   } else {
     if (NV == 1)
-      return VW == 4 ? pick_rv<R, 1, 4>(is_long, rowptr) : pick_rv<R, 1, 1>(is_long, rowptr);
-    return VW == 4 ? pick_rv<R, 2, 4>(is_long, rowptr) : pick_rv<R, 2, 1>(is_long, rowptr);
+      return VW == 4 ? pick_rv<R, 1, 4, TB>(is_long, rowptr) : pick_rv<R, 1, 1, TB>(is_long, rowptr);
+    return VW == 4 ? pick_rv<R, 2, 4, TB>(is_long, rowptr) : pick_rv<R, 2, 1, TB>(is_long, rowptr);
   }
 }
 
-KernelFn select_kernel(int R, int NV, int VW, bool is_long, bool rowptr) {
+template <class TB>
+KernelFn select_kernel_t(int R, int NV, int VW, bool is_long, bool rowptr) {
   switch (R) {
-    case 1: return pick_r<1>(NV, VW, is_long, rowptr);
-    case 2: return pick_r<2>(NV, VW, is_long, rowptr);
-    case 4: return pick_r<4>(NV, VW, is_long, rowptr);
-    case 8: return pick_r<8>(NV, VW, is_long, rowptr);
-    case 16: return pick_r<16>(NV, VW, is_long, rowptr);
+    case 1: return pick_r<1, TB>(NV, VW, is_long, rowptr);
+    case 2: return pick_r<2, TB>(NV, VW, is_long, rowptr);
+    case 4: return pick_r<4, TB>(NV, VW, is_long, rowptr);
+    case 8: return pick_r<8, TB>(NV, VW, is_long, rowptr);
+    case 16: return pick_r<16, TB>(NV, VW, is_long, rowptr);
   }
   return nullptr;
+}
+
+KernelFn select_kernel(int R, int NV, int VW, bool is_long, bool rowptr, bool bf16) {
+  return bf16 ? select_kernel_t<__nv_bfloat16>(R, NV, VW, is_long, rowptr)
+              : select_kernel_t<float>(R, NV, VW, is_long, rowptr);
 }
 
 int next_pow2(int x) {
@@ -744,7 +781,7 @@ vcsr_status resident_per_sm(KernelFn fn, int threads, size_t smem, int *per_sm) 
 }
 
 vcsr_status launch_one(KernelFn fn, const PanelDevView &P, long long team_items, int G,
-                       const LaunchShape &s, int chunk, size_t smem, const float *B, int ldb,
+                       const LaunchShape &s, int chunk, size_t smem, const void *B, int ldb,
                        float *C, int ldc, int O, cudaStream_t st) {
   const int threads = 256;
   int per_sm = 0;
@@ -761,15 +798,17 @@ vcsr_status launch_one(KernelFn fn, const PanelDevView &P, long long team_items,
 
 }  // namespace
 
-vcsr_status launch_panel_spmm(const PanelDevView &P, bool rowptr, const float *B, int ldb,
+vcsr_status launch_panel_spmm(const PanelDevView &P, bool rowptr, const void *B, int ldb,
                               float *C, int ldc, int O, cudaStream_t st, int *launches,
-                              cudaStream_t side, cudaEvent_t fork, cudaEvent_t join) {
+                              cudaStream_t side, cudaEvent_t fork, cudaEvent_t join,
+                              bool bf16) {
   if (launches) *launches = 0;
   const int n_short = rowptr ? P.n_units : P.n_batches;
   const int n_long = rowptr ? 0 : P.n_long;
   if (O <= 0 || n_short + n_long <= 0) return VCSR_OK;
+  // 128-bit lanes: four B values per load (16 bytes FP32, 8 bytes BF16)
   const bool vec4 = (O % 4 == 0) && (ldb % 4 == 0) && (ldc % 4 == 0) &&
-                    ((uintptr_t)B % 16 == 0) && ((uintptr_t)C % 16 == 0);
+                    ((uintptr_t)B % (bf16 ? 8 : 16) == 0) && ((uintptr_t)C % 16 == 0);
   const LaunchShape s = pick_shape(O, P.R, vec4);
   if (!rowptr && P.n_split_units > 0 && (O > P.pstride || s.n_otiles > P.counter_stride))
     return fail(VCSR_ERR_INVALID, "O=%d exceeds the plan's max_O=%d", O, P.pstride);
@@ -783,14 +822,14 @@ vcsr_status launch_panel_spmm(const PanelDevView &P, bool rowptr, const float *B
   }
   int n = 0;
   if (n_long > 0) {
-    KernelFn fl = select_kernel(P.R, s.NV, s.VW, true, false);
+    KernelFn fl = select_kernel(P.R, s.NV, s.VW, true, false, bf16);
     if (!fl) return fail(VCSR_ERR_UNSUPPORTED, "no kernel for R=%d", P.R);
     VCSR_TRY(launch_one(fl, P, n_long, G, s, chunk, smem, B, ldb, C, ldc, O,
                         both ? side : st));
     ++n;
   }
   if (n_short > 0) {
-    KernelFn fs = select_kernel(P.R, s.NV, s.VW, false, rowptr);
+    KernelFn fs = select_kernel(P.R, s.NV, s.VW, false, rowptr, bf16);
     if (!fs) return fail(VCSR_ERR_UNSUPPORTED, "no kernel for R=%d", P.R);
     VCSR_TRY(launch_one(fs, P, (n_short + G - 1) / G, G, s, chunk, smem, B, ldb, C, ldc, O,
                         st));

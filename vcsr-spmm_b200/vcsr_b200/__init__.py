@@ -115,6 +115,8 @@ _SIGS = {
     "vcsr_spmm_host": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
                                  C.c_void_p]),
     "vcsr_plan_check": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "vcsr_spmm_bf16": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int,
+                                 C.c_int, C.c_void_p, C.POINTER(C.c_int)]),
     "vcsr_plan_save": (C.c_int, [C.c_void_p, C.c_char_p]),
     "vcsr_plan_load": (C.c_int, [C.c_char_p, C.POINTER(C.c_void_p), C.c_void_p]),
     "vcsr_spmm_segmented": (C.c_int, [C.POINTER(_Vcsr), C.c_void_p, C.c_int, C.c_int,
@@ -492,8 +494,12 @@ class Plan:
         if ldc is None:
             ldc = Cout.stride(0) if hasattr(Cout, "stride") else O
         n = C.c_int(0)
-        _check(lib().vcsr_spmm(self._h, _ptr(B), ldb, _ptr(Cout), ldc, O,
-                               _stream(stream), C.byref(n)))
+        if str(getattr(B, "dtype", "")) == "torch.bfloat16":  # BF16 inputs, FP32 sums
+            _check(lib().vcsr_spmm_bf16(self._h, _ptr(B), ldb, _ptr(Cout), ldc, O,
+                                        _stream(stream), C.byref(n)))
+        else:
+            _check(lib().vcsr_spmm(self._h, _ptr(B), ldb, _ptr(Cout), ldc, O,
+                                   _stream(stream), C.byref(n)))
         self.last_launches = n.value
         return Cout
 
