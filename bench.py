@@ -67,6 +67,9 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="fem")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--size", type=int, default=None,
+                    help="override the workload's size parameter (rows, or the R-MAT "
+                         "scale); for small profiling captures")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-peers", action="store_true")
@@ -218,6 +221,8 @@ def cpu_reference(csr, B, seconds, min_reps=3):
 def build_inputs(args, rank, world):
     from vcsr_b200 import dist as D
     cfg, size, O, scaling, label = WORKLOADS[args.workload]
+    if args.size is not None:
+        size, label = args.size, f"{label}@size{args.size}"
     csr, row0, total = D.rank_panel(cfg, size, args.seed, rank, world, scaling, align=16)
     return csr, O, scaling, label, total
 
@@ -228,6 +233,8 @@ def run_reference(args):
         return
     import vcsr_b200 as V
     cfg, size, O, scaling, label = WORKLOADS[args.workload]
+    if args.size is not None:
+        size, label = args.size, f"{label}@size{args.size}"
     csr = V.gen_csr(cfg, args.seed, size)
     B = V.gen_dense_host(csr.N, O, args.seed + 1000, 0.0 if cfg == "rmat" else -1.0, 1.0)
     per_step = max(1.0, args.cpu_seconds / max(1, args.steps))

@@ -58,8 +58,9 @@ struct PanelHost {
 int choose_vec_rows(const vcsr_csr &csr, double *density_out);
 
 // Build the layout on the host for a given R (1, 2, 4, 8, 16).  chunk <= 0
-// picks union columns / (sms * 32) clamped to [256, 2048] so that a wave of sub-warps
-// holds many units while no unit is much longer than the average.
+// picks min(union columns / (sms * 32), max(512, 2 x average vector)) clamped
+// to [256, 2048], so that a wave of sub-warps holds many units and rows much
+// longer than the average (power-law hubs) are split over several warps.
 vcsr_status build_panel_host(const vcsr_csr &csr, int R, int chunk, int sms,
                              PanelHost *out);
 

@@ -199,6 +199,16 @@ constexpr int min_blocks_for() {
 #endif
 }
 
+// The long-unit kernel also runs the split fixup, so it keeps at most 2
+// blocks per SM, except R = 1 with two column vectors per lane (power-law
+// rows at O >= 256), measured faster at 3 (80 registers, no real spill:
+// R-MAT 2^22 at O = 256, 7.3 -> 6.5 ms).
+template <int R, int NV, int VW>
+constexpr int long_min_blocks_for() {
+  if (VW == 4 && R == 1 && NV == 2) return 3;
+  return min_blocks_for<R, NV, VW>() < 2 ? min_blocks_for<R, NV, VW>() : 2;
+}
+
 // Accumulators.  With 128-bit lanes the sums are kept as float2 pairs so that
 // one packed FFMA2 (__ffma2_rn: two round-to-nearest fused multiply-adds,
 // bit-identical to two fmaf) does two updates: pairs of rows (r, r+1) at one
@@ -617,9 +627,7 @@ __global__ void __launch_bounds__(256, (min_blocks_for<R, NV, VW>()))
 // Long work: a whole warp per long unit or split part, its sub-warps taking
 // every G-th union column; split parts finish through the part tickets.
 template <int R, int NV, int VW, class TB>
-__global__ void __launch_bounds__(256, (min_blocks_for<R, NV, VW>() < 2
-                                            ? min_blocks_for<R, NV, VW>()
-                                            : 2))
+__global__ void __launch_bounds__(256, (long_min_blocks_for<R, NV, VW>()))
     panel_long_kernel(const PanelDevView P, const void *__restrict__ Bv, int ldb,
                       float *__restrict__ C, int ldc, int O, int lshift, int n_otiles,
                       int W, int chunk) {
