@@ -285,7 +285,7 @@ def run_ours(args):
                               dist if world > 1 else None, dev)
     lo = 0.0 if WORKLOADS[args.workload][0] == "rmat" else -1.0
     tf32 = args.workload in TF32_WORKLOADS
-    plan = V.Plan(csr, segw=4, bundle=32, max_O=max(O, 512), tf32_panels=tf32)
+    plan = V.Plan(csr, segw=4, bundle=32, max_O=max(O, 512), tf32_panels=tf32, target_O=O)
     info = plan.info()
 
     # B: filled on rank 0, replicated by one NCCL broadcast (timed apart)

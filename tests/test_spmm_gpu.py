@@ -291,3 +291,19 @@ def test_repeat_runs_bitwise_identical():
     B = dB.cpu().numpy()
     ref = oracle.csr_spmm_f64(csr.M, csr.row_ptr, csr.col, csr.val, B)
     assert rel_l2(outs[0].cpu().numpy(), ref) <= TOL
+
+
+def test_target_o_picks_vector_height():
+    """target_O > 128 turns an automatic 8-row choice into 4 rows; results
+    stay within the FP32 tolerance either way; an explicit vec_rows wins."""
+    csr = V.gen_csr("fem", 0, 6000)
+    assert V.Plan(csr).info()["vec_rows"] == 8
+    assert V.Plan(csr, target_O=128).info()["vec_rows"] == 8
+    p = V.Plan(csr, target_O=512)
+    assert p.info()["vec_rows"] == 4
+    assert V.Plan(csr, target_O=512, vec_rows=8).info()["vec_rows"] == 8
+    B = V.gen_dense_host(csr.N, 256, 3)
+    C = torch.empty(csr.M, 256, device="cuda")
+    p.spmm(torch.from_numpy(B).cuda(), C)
+    ref = oracle.csr_spmm_f32(csr.M, csr.row_ptr, csr.col, csr.val, B)
+    assert rel_l2(C.cpu().numpy(), ref) <= TOL

@@ -175,6 +175,7 @@ void vcsr_plan_params_default(vcsr_plan_params *p) {
   p->chunk = 0;
   p->flags = 0;
   p->panel_min_nnz = 0;
+  p->target_O = 0;
 }
 
 vcsr_status vcsr_plan_create(const vcsr_csr *csr, int csr_where,
@@ -245,7 +246,10 @@ vcsr_status vcsr_plan_create(const vcsr_csr *csr, int csr_where,
   }
   vcsr::PanelHost ph;
   int R = params->vec_rows;
-  if (R == 0) R = vcsr::choose_vec_rows(work, nullptr);
+  if (R == 0) {
+    R = vcsr::choose_vec_rows(work, nullptr);
+    if (R == 8 && params->target_O > 128) R = 4;
+  }
   vcsr_status s = vcsr::build_panel_host(work, R, params->chunk, sms, &ph);
   if (s != VCSR_OK) {
     if (owned) vcsr_csr_free(&h, VCSR_HOST);

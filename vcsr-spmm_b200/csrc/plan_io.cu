@@ -24,7 +24,7 @@ using vcsr::fail;
 namespace {
 
 constexpr char kMagic[8] = {'V', 'C', 'S', 'R', 'P', 'L', 'A', 'N'};
-constexpr int64_t kVersion = 1;
+constexpr int64_t kVersion = 2;
 
 uint64_t fnv1a(const unsigned char *p, size_t n) {
   uint64_t h = 1469598103934665603ull;
@@ -149,7 +149,7 @@ vcsr_status vcsr_plan_save(const vcsr_plan *p, const char *path) {
         (int64_t)q.tileK, (int64_t)q.max_O, (int64_t)q.vec_rows, (int64_t)q.chunk,
         (int64_t)q.flags, (int64_t)q.panel_min_nnz, (int64_t)(p->has_ref ? 1 : 0),
         (int64_t)g.M, (int64_t)g.N, (int64_t)g.segw, (int64_t)g.bundle, (int64_t)g.num_groups,
-        (int64_t)g.num_segments, g.num_slots})
+        (int64_t)g.num_segments, g.num_slots, (int64_t)q.target_O})
     w.i64(v);
   w.arr(h.ucol); w.arr(h.uval); w.arr(h.units); w.arr(h.batches); w.arr(h.long_idx);
   w.arr(h.vec_ptr); w.arr(h.parts); w.arr(h.svecs); w.arr(h.rb_row); w.arr(h.rb_ptr);
@@ -196,7 +196,7 @@ vcsr_status vcsr_plan_load(const char *path, vcsr_plan **out, vcsr_stream_t stre
   if (!r.ok || version != kVersion || abi != VCSR_ABI_VERSION)
     return fail(VCSR_ERR_UNSUPPORTED, "plan file version %lld (ABI %lld); this library reads %lld (ABI %d)",
                 (long long)version, (long long)abi, (long long)kVersion, VCSR_ABI_VERSION);
-  int64_t hv[34];
+  int64_t hv[35];
   for (int64_t &v : hv) v = r.i64();
   if (!r.ok) return fail(VCSR_ERR_IO, "plan file %s is truncated", path);
   const int64_t M = hv[0], N = hv[1], nnz = hv[2], R = hv[3], nv = hv[4], nu = hv[5],
@@ -290,6 +290,7 @@ vcsr_status vcsr_plan_load(const char *path, vcsr_plan **out, vcsr_stream_t stre
   p->params.segw = (int)hv[18]; p->params.bundle = (int)hv[19]; p->params.tileK = (int)hv[20];
   p->params.max_O = (int)hv[21]; p->params.vec_rows = (int)hv[22]; p->params.chunk = (int)hv[23];
   p->params.flags = (int)hv[24]; p->params.panel_min_nnz = (int)hv[25];
+  p->params.target_O = (int)hv[34];
   cudaGetDevice(&p->device);
   for (int64_t j = 0; j < n_rp; ++j) {
     const int *q = &h.rpan[(size_t)j * 7];

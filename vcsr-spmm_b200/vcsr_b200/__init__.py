@@ -70,7 +70,7 @@ class _Vcsr(C.Structure):
 class _PlanParams(C.Structure):
     _fields_ = [("segw", C.c_int), ("bundle", C.c_int), ("tileK", C.c_int),
                 ("max_O", C.c_int), ("vec_rows", C.c_int), ("chunk", C.c_int),
-                ("flags", C.c_int), ("panel_min_nnz", C.c_int)]
+                ("flags", C.c_int), ("panel_min_nnz", C.c_int), ("target_O", C.c_int)]
 
 
 class _PlanInfo(C.Structure):
@@ -457,6 +457,7 @@ class Plan:
 
     def __init__(self, csr, segw=4, bundle=32, tileK=0, max_O=512, vec_rows=0,
                  chunk=0, reference_format=False, tf32_panels=False, panel_min_nnz=0,
+                 target_O=0,
                  stream=None):
         L = lib()
         p = _PlanParams()
@@ -466,6 +467,7 @@ class Plan:
         p.flags = ((PLAN_REFERENCE_FORMAT if reference_format else 0)
                    | (PLAN_TF32_PANELS if tf32_panels else 0))
         p.panel_min_nnz = panel_min_nnz
+        p.target_O = target_O
         where = DEVICE if isinstance(csr, DeviceCSR) else HOST
         s = csr._struct()
         h = C.c_void_p()
