@@ -246,6 +246,22 @@ vcsr_status vcsr_spmm(const vcsr_plan *plan, const float *dB, int ldb,
                       float *dC, int ldc, int O, vcsr_stream_t stream,
                       int *launches);
 
+/* Row panels of a plan (about equal nnz; at most 8), for callers that
+ * schedule the product themselves, e.g. behind a chunked broadcast of B: on
+ * input *count is the length of the arrays (any may be NULL; all NULL asks
+ * only for the count), on output the number of panels; panel j covers rows
+ * [row0[j], row1[j]) and reads B rows up to col_max[j] (-1: no entries).
+ * Plans with TF32 panels and small plans (M < 8192 or nnz < 2^20) have
+ * none.  No counterpart in the reference. */
+vcsr_status vcsr_plan_row_panels(const vcsr_plan *plan, int *count, int *row0, int *row1,
+                                 int *col_max);
+/* C rows of one row panel: C[row0[j]:row1[j]) = A[those rows] * B, with the
+ * contract of vcsr_spmm (the other rows of C are not touched).  The panels
+ * together are vcsr_spmm. */
+vcsr_status vcsr_spmm_row_panel(const vcsr_plan *plan, int panel, const float *dB, int ldb,
+                                float *dC, int ldc, int O, vcsr_stream_t stream,
+                                int *launches);
+
 /* C = A * B with B in BF16 (bfloat16 bits, N x O, leading dimension ldb);
  * each B value is widened to FP32 as it is loaded (exact) and the sums are the
  * FP32 path's, so C equals, bit for bit, vcsr_spmm on the widened B.  B traffic

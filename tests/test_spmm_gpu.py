@@ -307,3 +307,31 @@ def test_target_o_picks_vector_height():
     p.spmm(torch.from_numpy(B).cuda(), C)
     ref = oracle.csr_spmm_f32(csr.M, csr.row_ptr, csr.col, csr.val, B)
     assert rel_l2(C.cpu().numpy(), ref) <= TOL
+
+
+def test_row_panels_compose_the_product():
+    """vcsr_spmm_row_panel over all of a plan's row panels writes exactly
+    the product vcsr_spmm writes, bit for bit; other rows are left alone."""
+    for cfg, size in (("fem", 0), ("powerlaw", 0)):
+        csr = V.gen_csr(cfg, 1, size)
+        plan = V.Plan(csr)
+        panels = plan.row_panels()
+        assert panels and panels[0][0] == 0 and panels[-1][1] == csr.M
+        assert all(a[1] == b[0] for a, b in zip(panels[:-1], panels[1:]))
+        B = torch.randn(csr.N, 64, device="cuda")
+        C1 = torch.empty(csr.M, 64, device="cuda")
+        plan.spmm(B, C1)
+        C2 = torch.full((csr.M, 64), float("nan"), device="cuda")
+        for j in range(len(panels)):
+            plan.spmm_row_panel(j, B, C2)
+        torch.cuda.synchronize()
+        assert torch.equal(C1, C2)
+        C3 = torch.full((csr.M, 64), 7.0, device="cuda")
+        a, b, _ = panels[1]
+        plan.spmm_row_panel(1, B, C3)
+        torch.cuda.synchronize()
+        assert torch.equal(C3[a:b], C1[a:b]) and bool((C3[:a] == 7).all()) and bool((C3[b:] == 7).all())
+    with pytest.raises(V.VcsrError) as ei:
+        plan.spmm_row_panel(len(panels), B, C1)
+    assert ei.value.status == 8
+    assert V.Plan(V.gen_csr("fem", 0, 3000)).row_panels() == []  # small plans have none

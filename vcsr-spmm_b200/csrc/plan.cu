@@ -478,6 +478,48 @@ vcsr_status vcsr_spmm(const vcsr_plan *p, const float *dB, int ldb, float *dC,
   return VCSR_OK;
 }
 
+vcsr_status vcsr_plan_row_panels(const vcsr_plan *p, int *count, int *row0, int *row1,
+                                 int *col_max) {
+  vcsr::clear_error();
+  if (!p || !count) return fail(VCSR_ERR_INVALID, "null argument");
+  const int n = (int)p->rpanels.size();
+  if (row0 || row1 || col_max) {
+    if (*count < n) return fail(VCSR_ERR_INVALID, "arrays hold %d panels, the plan has %d", *count, n);
+    for (int j = 0; j < n; ++j) {
+      if (row0) row0[j] = p->rpanels[j].row0;
+      if (row1) row1[j] = p->rpanels[j].row1;
+      if (col_max) col_max[j] = p->rpanels[j].col_max;
+    }
+  }
+  *count = n;
+  return VCSR_OK;
+}
+
+vcsr_status vcsr_spmm_row_panel(const vcsr_plan *p, int panel, const float *dB, int ldb,
+                                float *dC, int ldc, int O, vcsr_stream_t stream,
+                                int *launches) {
+  vcsr::clear_error();
+  if (launches) *launches = 0;
+  if (!p) return fail(VCSR_ERR_INVALID, "null plan");
+  if (panel < 0 || panel >= (int)p->rpanels.size())
+    return fail(VCSR_ERR_RANGE, "row panel %d of %d", panel, (int)p->rpanels.size());
+  if (O < 0 || ldb < O || ldc < O)
+    return fail(VCSR_ERR_INVALID, "need 0 <= O <= ldb, ldc (O=%d ldb=%d ldc=%d)", O, ldb, ldc);
+  if (O == 0) return VCSR_OK;
+  if (!dC || !dB) return fail(VCSR_ERR_INVALID, "null B or C");
+  if (p->n_split_units > 0 && O > p->pstride)
+    return fail(VCSR_ERR_INVALID,
+                "O=%d exceeds the plan's max_O=%d (split rows need scratch)", O, p->pstride);
+  const auto &rp = p->rpanels[panel];
+  vcsr::PanelDevView v = view(p);
+  v.batches += rp.b0;
+  v.n_batches = rp.b1 - rp.b0;
+  v.long_idx += rp.l0;
+  v.n_long = rp.l1 - rp.l0;
+  return vcsr::launch_panel_spmm(v, false, dB, ldb, dC, ldc, O, (cudaStream_t)stream, launches,
+                                 p->side, p->fork, p->join);
+}
+
 vcsr_status vcsr_spmm_bf16(const vcsr_plan *p, const void *dB, int ldb, float *dC, int ldc,
                            int O, vcsr_stream_t stream, int *launches) {
   vcsr::clear_error();

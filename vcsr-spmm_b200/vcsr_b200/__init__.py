@@ -115,6 +115,10 @@ _SIGS = {
     "vcsr_spmm_host": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
                                  C.c_void_p]),
     "vcsr_plan_check": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "vcsr_plan_row_panels": (C.c_int, [C.c_void_p, C.POINTER(C.c_int), C.c_void_p,
+                                       C.c_void_p, C.c_void_p]),
+    "vcsr_spmm_row_panel": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p,
+                                      C.c_int, C.c_int, C.c_void_p, C.POINTER(C.c_int)]),
     "vcsr_spmm_bf16": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int,
                                  C.c_int, C.c_void_p, C.POINTER(C.c_int)]),
     "vcsr_plan_save": (C.c_int, [C.c_void_p, C.c_char_p]),
@@ -520,6 +524,32 @@ class Plan:
         self.M, self.N, self.nnz = i["M"], i["N"], i["nnz"]
         self.last_launches = 0
         return self
+
+    def row_panels(self):
+        """[(row0, row1, col_max)] of the plan's row panels (empty for small
+        plans and plans with TF32 panels)."""
+        n = C.c_int(0)
+        _check(lib().vcsr_plan_row_panels(self._h, C.byref(n), None, None, None))
+        if n.value == 0:
+            return []
+        r0, r1, cm = (np.zeros(n.value, np.int32) for _ in range(3))
+        _check(lib().vcsr_plan_row_panels(self._h, C.byref(n), r0.ctypes.data, r1.ctypes.data,
+                                          cm.ctypes.data))
+        return [(int(a), int(b), int(c)) for a, b, c in zip(r0, r1, cm)]
+
+    def spmm_row_panel(self, panel, B, Cout, O=None, ldb=None, ldc=None, stream=None):
+        """Rows of one row panel of C = A*B (vcsr_spmm_row_panel)."""
+        if O is None:
+            O = B.shape[1]
+        if ldb is None:
+            ldb = B.stride(0) if hasattr(B, "stride") else O
+        if ldc is None:
+            ldc = Cout.stride(0) if hasattr(Cout, "stride") else O
+        n = C.c_int(0)
+        _check(lib().vcsr_spmm_row_panel(self._h, panel, _ptr(B), ldb, _ptr(Cout), ldc, O,
+                                         _stream(stream), C.byref(n)))
+        self.last_launches = n.value
+        return Cout
 
     def check(self, stream=None):
         """Synchronise and raise VcsrError (status 7) if a bounded wait of the
