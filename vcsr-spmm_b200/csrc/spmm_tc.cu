@@ -245,8 +245,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       long long g = 0;
       int lt = 0;  // local item count
       for (int t = blockIdx.x; t < n_items && !*abort_flag; t += gridDim.x, ++lt) {
-        const int oc = t / V.n_rb, rbi = t - oc * V.n_rb;
-        (void)oc;
+        const int rbi = t % V.n_rb;  // items run over row blocks within each slice
         const int nblk = V.rb_ptr[rbi + 1] - V.rb_ptr[rbi];
         const int buf = lt & 1;
         if (lt >= 2 && !mbar_wait(dfree + buf, (uint32_t)(((lt - 2) >> 1) & 1), abort_flag,
