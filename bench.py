@@ -17,6 +17,7 @@ Workloads (synthetic stand-ins with the benchmark configurations' shapes):
                  tensor cores in TF32 (VCSR_PLAN_TF32_PANELS).
   rmat_bf16, fem_bf16  B held in bfloat16, widened to FP32 on load
                  (vcsr_spmm_bf16): half the B bytes, FP32 sums.
+  rmat_f16, fem_f16  the same with B in float16 (vcsr_spmm_f16).
   rmat           2^22 R-MAT, O = 256: A cut into N nnz-balanced row panels,
                  B broadcast once: strong scaling.
 
@@ -52,11 +53,14 @@ WORKLOADS = {
     "rmat": ("rmat", 22, 256, "strong", "rmat_s22_O256"),
     "rmat_bf16": ("rmat", 22, 256, "strong", "rmat_s22_O256_bf16in"),
     "fem_bf16": ("fem", 0, 128, "weak", "fem_banded_62451_O128_bf16in"),
+    "rmat_f16": ("rmat", 22, 256, "strong", "rmat_s22_O256_f16in"),
+    "fem_f16": ("fem", 0, 128, "weak", "fem_banded_62451_O128_f16in"),
 }
 # workloads whose dense 16x16 blocks run on the tcgen05 TF32 path
 TF32_WORKLOADS = {"blockdense_tf32"}
-# workloads whose B is held in bfloat16 (FP32 sums: vcsr_spmm_bf16)
-BF16_WORKLOADS = {"rmat_bf16", "fem_bf16"}
+# workloads whose B is held in a 16-bit type (FP32 sums: vcsr_spmm_bf16 / _f16)
+HALF_WORKLOADS = {"rmat_bf16": "bfloat16", "fem_bf16": "bfloat16",
+                  "rmat_f16": "float16", "fem_f16": "float16"}
 
 
 def parse():
@@ -293,11 +297,12 @@ def run_ours(args):
     bcast_ms = None
     if rank == 0 or world == 1:
         V.gen_dense_device(dB, args.seed + 1000, lo, 1.0)
-    bf16 = args.workload in BF16_WORKLOADS
+    half = HALF_WORKLOADS.get(args.workload)
+    bf16 = half is not None  # any 16-bit B
     dB32 = dB  # FP32 copy for the peers and the CPU baseline
     if bf16:
-        dB32 = dB.to(torch.bfloat16).float()  # the values the BF16 path sees
-        dB = dB.to(torch.bfloat16)
+        dB32 = dB.to(getattr(torch, half)).float()  # the values the 16-bit path sees
+        dB = dB.to(getattr(torch, half))
     if world > 1:
         torch.cuda.synchronize()
         if bf16:
@@ -454,7 +459,7 @@ def run_ours(args):
             "metric": METRIC, "value": round(value, 3), "unit": "GFLOP/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms_step, 5), "higher_is_better": True,
-            "scaling": scaling, "vs_baseline": None, "dtype": "tf32" if tf32 else ("bf16-in/f32-acc" if bf16 else "f32"),
+            "scaling": scaling, "vs_baseline": None, "dtype": "tf32" if tf32 else ({"bfloat16": "bf16", "float16": "f16"}[half] + "-in/f32-acc" if bf16 else "f32"),
             "data": "synthetic",
             "config": {"workload": label, "M": csr.M, "N": csr.N, "nnz": csr.nnz,
                        "global_nnz": global_nnz, "O": O, "segw": 4, "bundle": 32,

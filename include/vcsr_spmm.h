@@ -273,6 +273,15 @@ vcsr_status vcsr_spmm_bf16(const vcsr_plan *plan, const void *dB, int ldb,
                            float *dC, int ldc, int O, vcsr_stream_t stream,
                            int *launches);
 
+/* The same with B in FP16 (IEEE binary16 bits): each value is widened to FP32
+ * as it is loaded (exact, subnormals included), FP32 sums, so C equals, bit for
+ * bit, vcsr_spmm on the widened B.  Same rules as vcsr_spmm_bf16.  The
+ * reference's FP16 kernel (src/vcsr_tc.cu:122-195) rounds A to FP16 as well
+ * and sums on the tensor cores; this one keeps A in FP32. */
+vcsr_status vcsr_spmm_f16(const vcsr_plan *plan, const void *dB, int ldb,
+                          float *dC, int ldc, int O, vcsr_stream_t stream,
+                          int *launches);
+
 /* The same product with host buffers: copies hB (N x O, ld = O) to the device,
  * runs vcsr_spmm, copies C back to hC (M x O, ld = O) and synchronises the
  * stream.  Replaces the upload/launch/download sequence of the reference's

@@ -520,8 +520,11 @@ vcsr_status vcsr_spmm_row_panel(const vcsr_plan *p, int panel, const float *dB, 
                                  p->side, p->fork, p->join);
 }
 
-vcsr_status vcsr_spmm_bf16(const vcsr_plan *p, const void *dB, int ldb, float *dC, int ldc,
-                           int O, vcsr_stream_t stream, int *launches) {
+namespace {
+
+// vcsr_spmm with B of a 16-bit element type (bt), widened as it is loaded.
+vcsr_status spmm_16bit(const vcsr_plan *p, const void *dB, int ldb, float *dC, int ldc, int O,
+                       vcsr_stream_t stream, int *launches, vcsr::BType bt, const char *name) {
   vcsr::clear_error();
   if (launches) *launches = 0;
   if (!p) return fail(VCSR_ERR_INVALID, "null plan");
@@ -531,12 +534,24 @@ vcsr_status vcsr_spmm_bf16(const vcsr_plan *p, const void *dB, int ldb, float *d
   if (!dC || (!dB && p->N > 0)) return fail(VCSR_ERR_INVALID, "null B or C");
   if (p->n_panel_rb > 0)
     return fail(VCSR_ERR_UNSUPPORTED, "a plan with TF32 panels reads B in FP32");
-  if ((uintptr_t)dB % 2) return fail(VCSR_ERR_INVALID, "BF16 B must be 2-byte aligned");
+  if ((uintptr_t)dB % 2) return fail(VCSR_ERR_INVALID, "%s B must be 2-byte aligned", name);
   if (p->n_split_units > 0 && O > p->pstride)
     return fail(VCSR_ERR_INVALID,
                 "O=%d exceeds the plan's max_O=%d (split rows need scratch)", O, p->pstride);
   return vcsr::launch_panel_spmm(view(p), false, dB, ldb, dC, ldc, O, (cudaStream_t)stream,
-                                 launches, p->side, p->fork, p->join, true);
+                                 launches, p->side, p->fork, p->join, bt);
+}
+
+}  // namespace
+
+vcsr_status vcsr_spmm_bf16(const vcsr_plan *p, const void *dB, int ldb, float *dC, int ldc,
+                           int O, vcsr_stream_t stream, int *launches) {
+  return spmm_16bit(p, dB, ldb, dC, ldc, O, stream, launches, vcsr::BType::kBF16, "BF16");
+}
+
+vcsr_status vcsr_spmm_f16(const vcsr_plan *p, const void *dB, int ldb, float *dC, int ldc,
+                          int O, vcsr_stream_t stream, int *launches) {
+  return spmm_16bit(p, dB, ldb, dC, ldc, O, stream, launches, vcsr::BType::kF16, "FP16");
 }
 
 vcsr_status vcsr_spmm_host(vcsr_plan *p, const float *hB, float *hC, int O,

@@ -30,6 +30,10 @@ struct PanelDevView {
   int R = 1;
 };
 
+// Element type of B: FP32 as stored, or 16-bit values widened to FP32 as they
+// are loaded (exactly), the sums being FP32 either way.
+enum class BType { kF32, kBF16, kF16 };
+
 struct LaunchShape {
   int VW;        // floats per access: 4 (128-bit) or 1
   int NV;        // accesses per lane per O-tile
@@ -48,6 +52,7 @@ LaunchShape pick_shape(int O, int R, bool vec4);
 vcsr_status launch_panel_spmm(const PanelDevView &P, bool rowptr,
                               const void *B, int ldb, float *C, int ldc, int O,
                               cudaStream_t st, int *launches, cudaStream_t side,
-                              cudaEvent_t fork, cudaEvent_t join, bool bf16 = false);
+                              cudaEvent_t fork, cudaEvent_t join,
+                              BType bt = BType::kF32);
 
 }  // namespace vcsr

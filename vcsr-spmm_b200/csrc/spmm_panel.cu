@@ -28,6 +28,7 @@
 #include <cuda_runtime.h>
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include <mutex>
 #include <utility>
@@ -86,8 +87,8 @@ struct VecT<1> {
 };
 
 // B values widened to FP32 as they are loaded: FP32 as stored; BF16 by
-// placing its 16 bits in the high half of a float (exact), four values per
-// 8-byte load with 128-bit lanes.
+// placing its 16 bits in the high half of a float, FP16 by the half-to-float
+// conversion (both exact), four values per 8-byte load with 128-bit lanes.
 template <int VW>
 struct LdB;
 template <>
@@ -100,12 +101,21 @@ struct LdB<4> {
     return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
                        __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u));
   }
+  static __device__ __forceinline__ float4 ld(const __half *p) {
+    const uint2 u = __ldg(reinterpret_cast<const uint2 *>(p));
+    const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+  }
 };
 template <>
 struct LdB<1> {
   static __device__ __forceinline__ float ld(const float *p) { return __ldg(p); }
   static __device__ __forceinline__ float ld(const __nv_bfloat16 *p) {
     return __uint_as_float((unsigned)__ldg(reinterpret_cast<const unsigned short *>(p)) << 16);
+  }
+  static __device__ __forceinline__ float ld(const __half *p) {
+    return __half2float(__ushort_as_half(__ldg(reinterpret_cast<const unsigned short *>(p))));
   }
 };
 
@@ -702,9 +712,12 @@ KernelFn select_kernel_t(int R, int NV, int VW, bool is_long, bool rowptr) {
   return nullptr;
 }
 
-KernelFn select_kernel(int R, int NV, int VW, bool is_long, bool rowptr, bool bf16) {
-  return bf16 ? select_kernel_t<__nv_bfloat16>(R, NV, VW, is_long, rowptr)
-              : select_kernel_t<float>(R, NV, VW, is_long, rowptr);
+KernelFn select_kernel(int R, int NV, int VW, bool is_long, bool rowptr, BType bt) {
+  switch (bt) {
+    case BType::kBF16: return select_kernel_t<__nv_bfloat16>(R, NV, VW, is_long, rowptr);
+    case BType::kF16: return select_kernel_t<__half>(R, NV, VW, is_long, rowptr);
+    default: return select_kernel_t<float>(R, NV, VW, is_long, rowptr);
+  }
 }
 
 int next_pow2(int x) {
@@ -809,14 +822,14 @@ vcsr_status launch_one(KernelFn fn, const PanelDevView &P, long long team_items,
 vcsr_status launch_panel_spmm(const PanelDevView &P, bool rowptr, const void *B, int ldb,
                               float *C, int ldc, int O, cudaStream_t st, int *launches,
                               cudaStream_t side, cudaEvent_t fork, cudaEvent_t join,
-                              bool bf16) {
+                              BType bt) {
   if (launches) *launches = 0;
   const int n_short = rowptr ? P.n_units : P.n_batches;
   const int n_long = rowptr ? 0 : P.n_long;
   if (O <= 0 || n_short + n_long <= 0) return VCSR_OK;
-  // 128-bit lanes: four B values per load (16 bytes FP32, 8 bytes BF16)
+  // 128-bit lanes: four B values per load (16 bytes FP32, 8 bytes BF16 / FP16)
   const bool vec4 = (O % 4 == 0) && (ldb % 4 == 0) && (ldc % 4 == 0) &&
-                    ((uintptr_t)B % (bf16 ? 8 : 16) == 0) && ((uintptr_t)C % 16 == 0);
+                    ((uintptr_t)B % (bt == BType::kF32 ? 16 : 8) == 0) && ((uintptr_t)C % 16 == 0);
   const LaunchShape s = pick_shape(O, P.R, vec4);
   if (!rowptr && P.n_split_units > 0 && (O > P.pstride || s.n_otiles > P.counter_stride))
     return fail(VCSR_ERR_INVALID, "O=%d exceeds the plan's max_O=%d", O, P.pstride);
@@ -830,14 +843,14 @@ vcsr_status launch_panel_spmm(const PanelDevView &P, bool rowptr, const void *B,
   }
   int n = 0;
   if (n_long > 0) {
-    KernelFn fl = select_kernel(P.R, s.NV, s.VW, true, false, bf16);
+    KernelFn fl = select_kernel(P.R, s.NV, s.VW, true, false, bt);
     if (!fl) return fail(VCSR_ERR_UNSUPPORTED, "no kernel for R=%d", P.R);
     VCSR_TRY(launch_one(fl, P, n_long, G, s, chunk, smem, B, ldb, C, ldc, O,
                         both ? side : st));
     ++n;
   }
   if (n_short > 0) {
-    KernelFn fs = select_kernel(P.R, s.NV, s.VW, false, rowptr, bf16);
+    KernelFn fs = select_kernel(P.R, s.NV, s.VW, false, rowptr, bt);
     if (!fs) return fail(VCSR_ERR_UNSUPPORTED, "no kernel for R=%d", P.R);
     VCSR_TRY(launch_one(fs, P, (n_short + G - 1) / G, G, s, chunk, smem, B, ldb, C, ldc, O,
                         st));

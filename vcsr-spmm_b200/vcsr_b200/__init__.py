@@ -121,6 +121,8 @@ _SIGS = {
                                       C.c_int, C.c_int, C.c_void_p, C.POINTER(C.c_int)]),
     "vcsr_spmm_bf16": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int,
                                  C.c_int, C.c_void_p, C.POINTER(C.c_int)]),
+    "vcsr_spmm_f16": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int,
+                                C.c_int, C.c_void_p, C.POINTER(C.c_int)]),
     "vcsr_plan_save": (C.c_int, [C.c_void_p, C.c_char_p]),
     "vcsr_plan_load": (C.c_int, [C.c_char_p, C.POINTER(C.c_void_p), C.c_void_p]),
     "vcsr_spmm_segmented": (C.c_int, [C.POINTER(_Vcsr), C.c_void_p, C.c_int, C.c_int,
@@ -492,7 +494,8 @@ class Plan:
         return _vcsr_from_host_struct(v)
 
     def spmm(self, B, Cout, O=None, ldb=None, ldc=None, stream=None):
-        """C = A*B on device tensors (or raw pointers with O/ldb/ldc given)."""
+        """C = A*B on device tensors (or raw pointers with O/ldb/ldc given).
+        A bfloat16 or float16 B runs vcsr_spmm_bf16 / vcsr_spmm_f16 (FP32 C)."""
         if O is None:
             O = B.shape[1]
         if ldb is None:
@@ -500,9 +503,13 @@ class Plan:
         if ldc is None:
             ldc = Cout.stride(0) if hasattr(Cout, "stride") else O
         n = C.c_int(0)
-        if str(getattr(B, "dtype", "")) == "torch.bfloat16":  # BF16 inputs, FP32 sums
+        dt = str(getattr(B, "dtype", ""))
+        if dt == "torch.bfloat16":  # 16-bit inputs, FP32 sums
             _check(lib().vcsr_spmm_bf16(self._h, _ptr(B), ldb, _ptr(Cout), ldc, O,
                                         _stream(stream), C.byref(n)))
+        elif dt == "torch.float16":
+            _check(lib().vcsr_spmm_f16(self._h, _ptr(B), ldb, _ptr(Cout), ldc, O,
+                                       _stream(stream), C.byref(n)))
         else:
             _check(lib().vcsr_spmm(self._h, _ptr(B), ldb, _ptr(Cout), ldc, O,
                                    _stream(stream), C.byref(n)))
