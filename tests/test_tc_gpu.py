@@ -65,6 +65,28 @@ def test_tf32_panels_exact_small_integers():
     assert np.array_equal(dC.cpu().numpy(), (A.astype(np.float64) @ B).astype(np.float32))
 
 
+@pytest.mark.parametrize("O,ldb", [(96, 96), (160, 160), (64, 72), (256, 260), (100, 104)])
+def test_tf32_panels_exact_b_views(O, ldb):
+    # O a multiple of 32 reads B through the 3-D slab view (one copy per slab),
+    # partial last 128-column slices (96, 160) and padded rows (ldb > O)
+    # included; O = 100 through the 2-D view.  Small integers: exact.
+    rng = np.random.default_rng(O + ldb)
+    A = np.zeros((96, 112), np.float32)
+    for bi, bj in [(0, 1), (1, 6), (2, 0), (2, 3), (5, 6), (4, 2)]:
+        A[16 * bi:16 * bi + 16, 16 * bj:16 * bj + 16] = rng.integers(-3, 4, (16, 16))
+    A[7, 100] = 3.0
+    Bfull = rng.integers(-4, 5, (112, ldb)).astype(np.float32)
+    csr = csr_from_dense(A)
+    plan = V.Plan(csr, tf32_panels=True, max_O=512, panel_min_nnz=2)
+    assert plan.info()["num_panel_blocks"] == 6
+    dB = torch.from_numpy(Bfull).cuda()
+    dC = torch.full((96, O), float("nan"), device="cuda")
+    plan.spmm(dB, dC, O=O, ldb=ldb, ldc=O)
+    plan.check()
+    want = (A.astype(np.float64) @ Bfull[:, :O]).astype(np.float32)
+    assert np.array_equal(dC.cpu().numpy(), want)
+
+
 @pytest.mark.parametrize("O", [128, 64, 100, 256])
 def test_tf32_panels_blockdense(O):
     csr = V.gen_csr("blockdense", 0, 4096)

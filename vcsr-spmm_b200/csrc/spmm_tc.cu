@@ -28,7 +28,10 @@
 // mbarriers); lane 0 of warp 5 issues the MMAs.  The producer runs up to
 // kStages * kG blocks ahead of the MMAs.  Measured on B200 the copy issue
 // rate of the SM's TMA unit (about 46 cycles per 2-KB box) bounds this
-// kernel; grouping blocks per stage saves barrier round trips.  Two
+// kernel; grouping blocks per stage saves barrier round trips, and when O is
+// a multiple of 32 a 3-D view of B (32 floats, rows, 32-float chunks) brings
+// a slab's four boxes in with one copy that lands them at the same swizzled
+// addresses.  Two
 // accumulators alternate between items so the epilogue of item t runs while
 // the MMAs of item t+1 are issued.  Every mbarrier wait is bounded: after
 // ~2^22 polls the kernel records which wait gave up and stops; before it
@@ -116,6 +119,17 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *tm, in
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
       "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
       "l"(tm), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Box {32, 16, 4} of the 3-D view: chunk-major, each chunk's 16 rows of 128
+// bytes together, as four 2-D boxes placed 2 KB apart would be.
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *tm, int x, int y,
+                                            int z, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+      "l"(tm), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
       : "memory");
 }
 
@@ -228,10 +242,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_add_tx(full + s, kBlockBytes);
           bulk_load(st + kG * kBTileBytes + u * kABlockBytes, V.blk_val + (size_t)bi * 256,
                     kABlockBytes, full + s);
+          if (V.slab3d) {
+            tma_load_3d(st + u * kBTileBytes, &tmB, 0, 16 * j, oc * 4, full + s);
+          } else {
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
-            tma_load_2d(st + u * kBTileBytes + q * 2048, &tmB, oc * 128 + 32 * q, 16 * j,
-                        full + s);
+            for (int q = 0; q < 4; ++q)
+              tma_load_2d(st + u * kBTileBytes + q * 2048, &tmB, oc * 128 + 32 * q, 16 * j,
+                          full + s);
+          }
           ++g_load;
           if (u == kG - 1) mbar_arrive(full + s);
         }
@@ -389,15 +407,32 @@ vcsr_status launch_tc_panels(const TcView &V0, const float *B, int N, int ldb, f
   EncodeTiledFn enc;
   VCSR_TRY(encode_fn(&enc));
   CUtensorMap tm;
-  const cuuint64_t dims[2] = {(cuuint64_t)O, (cuuint64_t)N};
-  const cuuint64_t strides[1] = {(cuuint64_t)ldb * 4};
-  const cuuint32_t box[2] = {32, 16};
-  const cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)B, dims, strides, box,
-                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  // With O a multiple of 32 the 3-D view {32 floats, N rows, O/32 chunks}
+  // (strides ldb*4 and 128 bytes) covers exactly B's N x O values: every
+  // in-range coordinate addresses inside B, and chunks past O/32 (a partial
+  // last 128-column slice) read as zeros.  Otherwise the 2-D view {O, N}
+  // with boxes of 32 x 16 zero-fills past O.
+  const bool slab3d = (O % 32) == 0;
+  CUresult r;
+  const cuuint32_t estr[3] = {1, 1, 1};
+  if (slab3d) {
+    const cuuint64_t dims[3] = {32, (cuuint64_t)N, (cuuint64_t)(O / 32)};
+    const cuuint64_t strides[2] = {(cuuint64_t)ldb * 4, 128};
+    const cuuint32_t box[3] = {32, 16, 4};
+    r = enc(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void *)B, dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    const cuuint64_t dims[2] = {(cuuint64_t)O, (cuuint64_t)N};
+    const cuuint64_t strides[1] = {(cuuint64_t)ldb * 4};
+    const cuuint32_t box[2] = {32, 16};
+    r = enc(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)B, dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
   if (r != CUDA_SUCCESS) return fail(VCSR_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   TcView V = V0;
+  V.slab3d = slab3d ? 1 : 0;
   V.O = O;
   V.ldc = ldc;
   V.C = C;

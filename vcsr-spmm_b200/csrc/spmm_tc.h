@@ -21,6 +21,9 @@ struct TcView {
   const int *blk_col = nullptr;
   const float *blk_val = nullptr;
   int M = 0, O = 0, ldc = 0, n_ochunks = 0;
+  // B's tensor map is 3-D (32 floats, rows, 32-float chunks): one copy per
+  // slab instead of four (set by the launcher when O is a multiple of 32)
+  int slab3d = 0;
   float *C = nullptr;
   // first failure: wait site (1 stage full, 2 stage empty, 3 accumulator
   // full, 4 accumulator free) | block index << 4; 0 when none
