@@ -239,9 +239,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           unsigned char *st = stage + s * kStageBytes;
           const int j = V.blk_col[bi];
-          mbar_add_tx(full + s, kBlockBytes);
-          bulk_load(st + kG * kBTileBytes + u * kABlockBytes, V.blk_val + (size_t)bi * 256,
-                    kABlockBytes, full + s);
+          // the values of a run of blocks that stays in this item and this
+          // stage are contiguous on both sides: one bulk copy at its start,
+          // its bytes expected before it is issued
+          const int run = (u == 0 || bi == b0) ? min(kG - u, b1 - bi) : 0;
+          mbar_add_tx(full + s, (uint32_t)(kBTileBytes + run * kABlockBytes));
+          if (run > 0)
+            bulk_load(st + kG * kBTileBytes + u * kABlockBytes, V.blk_val + (size_t)bi * 256,
+                      (uint32_t)(run * kABlockBytes), full + s);
           if (V.slab3d) {
             tma_load_3d(st + u * kBTileBytes, &tmB, 0, 16 * j, oc * 4, full + s);
           } else {
