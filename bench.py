@@ -363,6 +363,20 @@ def run_ours(args):
     achieved = abytes / (avg_ms * 1e-3) / 1e9
     peak, peak_kind = peaks()
     traffic = profile_traffic(label) if world == 1 else None
+    # the FP32 kernels' other bound: FMA issue.  Useful = 2*nnz*O of this
+    # rank; slots = 2*union*R*O, the FMAs the vector panels issue (zeros of a
+    # vector's rows included); peak = SMs x 128 FP32 lanes x 2 x max SM clock
+    fp32 = None
+    if not tf32:
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        mhz = (clk or {}).get("sm_max_mhz") or 1965.0
+        fpk = sms * 128 * 2 * mhz * 1e6 / 1e12
+        useful = 2.0 * csr.nnz * O / (avg_ms * 1e-3) / 1e12
+        slots = 2.0 * info["num_union"] * info["vec_rows"] * O / (avg_ms * 1e-3) / 1e12
+        fp32 = {"useful_tflops": round(useful, 2), "slot_tflops": round(slots, 2),
+                "peak_tflops": round(fpk, 1),
+                "peak_kind": "nominal: SMs x 128 FP32 lanes x 2 x max SM clock",
+                "frac_useful": round(useful / fpk, 4), "frac_slots": round(slots / fpk, 4)}
 
     # several GPUs: B's broadcast overlapped with the product (row panels
     # multiplied as their chunk of B arrives), timed like the step: max over
@@ -476,7 +490,7 @@ def run_ours(args):
                          "frac": round(achieved / peak, 4), "traffic": traffic,
                          "peak_kind": peak_kind,
                          "algorithmic_bytes": int(abytes),
-                         "kernel_ms": round(avg_ms, 5)},
+                         "kernel_ms": round(avg_ms, 5), "fp32_fma": fp32},
             "gpu_launches": int(launches),
             "e2e": e2e, "clocks": clk, "cpu_baseline": cpu, "peers": peers,
             "build_ms": round(info["build_ms"], 1),
