@@ -402,11 +402,11 @@ def run_ours(args):
         hB = torch.empty(csr.N, O, dtype=torch.float32, pin_memory=True)
         hB.copy_(dB32.cpu())
         hC = torch.empty(csr.M, O, dtype=torch.float32, pin_memory=True)
-        for _ in range(max(1, min(3, args.warmup))):
+        for _ in range(max(3, min(5, args.warmup))):
             plan.spmm_host(hB.numpy(), hC.numpy(), stream=stream)
         if world > 1:
             dist.barrier()
-        n_e2e = max(3, min(args.steps, 10))
+        n_e2e = max(5, min(args.steps, 20))
         t0 = time.perf_counter()
         for _ in range(n_e2e):
             plan.spmm_host(hB.numpy(), hC.numpy(), stream=stream)

@@ -286,10 +286,11 @@ vcsr_status vcsr_spmm_f16(const vcsr_plan *plan, const void *dB, int ldb,
  * runs vcsr_spmm, copies C back to hC (M x O, ld = O) and synchronises the
  * stream.  Replaces the upload/launch/download sequence of the reference's
  * main (src/main.cpp:104-161) as one call.  With more than 8 MB of B and C
- * the transfers overlap the work: for banded matrices (every row panel reads
- * B rows of at most the next upload chunk) B goes up in row chunks, each row
- * panel runs as soon as its B rows are on the device and its C rows come
- * back while later chunks go up; otherwise, with O >= 128, up to four column
+ * the transfers overlap the work: for banded matrices (no row panel reads B
+ * rows beyond the next 1/8 of B) B goes up in row chunks cut at the highest
+ * column of each row panel, each row panel runs as soon as its chunk is on
+ * the device and its C rows come back while later chunks go up; otherwise,
+ * with O >= 128, up to four column
  * chunks form the pipeline (chunk k comes back while chunk k+1 goes up).
  * Downloads and products run on plan-owned streams; the call returns after
  * all of them.  Host buffers should be pinned for full PCIe speed and for
