@@ -657,9 +657,11 @@ vcsr_status vcsr_spmm_host(vcsr_plan *p, const float *hB, float *hC, int O,
   }
   // Columns of B and C split into chunks are independent products
   // (C[:, chunk] = A * B[:, chunk]).  With large buffers the call runs as a
-  // pipeline of up to four chunks: chunk k is uploaded and multiplied on
-  // `stream`, then downloaded on the plan's download stream while chunk k+1
-  // is uploaded, so the two PCIe directions overlap.  Chunk copies are 2-D
+  // pipeline of up to four chunks: the chunks go up back to back on
+  // `stream`, chunk k is multiplied on the plan's compute stream once it is
+  // up and downloaded on the plan's download stream once multiplied, so the
+  // two PCIe directions overlap and no upload waits for a product.  Chunk
+  // copies are 2-D
   // (w floats out of every row of O); measured on B200 hosts, rows of at
   // least 256 bytes keep both directions at full speed (128-byte rows lose
   // a third), so a chunk is at least 64 floats wide.
@@ -677,38 +679,46 @@ vcsr_status vcsr_spmm_host(vcsr_plan *p, const float *hB, float *hC, int O,
     return p->d_err ? vcsr_plan_check(p, stream) : VCSR_OK;
   }
   if (!p->down) VCSR_CUDA(cudaStreamCreateWithFlags(&p->down, cudaStreamNonBlocking));
-  while ((int)p->chunk_done.size() < n_chunks) {
+  if (!p->comp) VCSR_CUDA(cudaStreamCreateWithFlags(&p->comp, cudaStreamNonBlocking));
+  while ((int)p->chunk_done.size() < 2 * n_chunks) {
     cudaEvent_t e;
     VCSR_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
     p->chunk_done.push_back(e);
   }
   const size_t pitch = sizeof(float) * (size_t)O;
   vcsr_status status = VCSR_OK;
-  for (int k = 0; k < n_chunks && status == VCSR_OK; ++k) {
+  cudaError_t e = cudaSuccess;
+  for (int k = 0; k < n_chunks && e == cudaSuccess; ++k) {  // uploads, back to back
     const int o0 = k * W, w = std::min(W, O - o0);
-    cudaError_t e = cudaSuccess;
     if (p->N > 0)
       e = cudaMemcpy2DAsync(p->d_stage_B + o0, pitch, hB + o0, pitch, sizeof(float) * w,
                             (size_t)p->N, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaEventRecord(p->chunk_done[k], st);
+  }
+  if (e != cudaSuccess) status = fail(VCSR_ERR_CUDA, "chunk upload: %s", cudaGetErrorString(e));
+  for (int k = 0; k < n_chunks && status == VCSR_OK; ++k) {
+    const int o0 = k * W, w = std::min(W, O - o0);
+    e = cudaStreamWaitEvent(p->comp, p->chunk_done[k], 0);
     if (e != cudaSuccess) {
-      status = fail(VCSR_ERR_CUDA, "chunk upload: %s", cudaGetErrorString(e));
+      status = fail(VCSR_ERR_CUDA, "chunk wait: %s", cudaGetErrorString(e));
       break;
     }
-    status = vcsr_spmm(p, p->d_stage_B + o0, O, p->d_stage_C + o0, O, w, stream, nullptr);
+    status = vcsr_spmm(p, p->d_stage_B + o0, O, p->d_stage_C + o0, O, w, p->comp, nullptr);
     if (status != VCSR_OK) break;
-    e = cudaEventRecord(p->chunk_done[k], st);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(p->down, p->chunk_done[k], 0);
+    e = cudaEventRecord(p->chunk_done[n_chunks + k], p->comp);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(p->down, p->chunk_done[n_chunks + k], 0);
     if (e == cudaSuccess && p->M > 0)
       e = cudaMemcpy2DAsync(hC + o0, pitch, p->d_stage_C + o0, pitch, sizeof(float) * w,
                             (size_t)p->M, cudaMemcpyDeviceToHost, p->down);
     if (e != cudaSuccess) status = fail(VCSR_ERR_CUDA, "chunk download: %s", cudaGetErrorString(e));
   }
-  // both streams drain before returning, also after an error
+  // every stream drains before returning, also after an error
+  const cudaError_t e0 = cudaStreamSynchronize(p->comp);
   const cudaError_t e1 = cudaStreamSynchronize(p->down), e2 = cudaStreamSynchronize(st);
   if (status != VCSR_OK) return status;
-  if (e1 != cudaSuccess || e2 != cudaSuccess)
+  if (e0 != cudaSuccess || e1 != cudaSuccess || e2 != cudaSuccess)
     return fail(VCSR_ERR_CUDA, "host entry point: %s",
-                cudaGetErrorString(e1 != cudaSuccess ? e1 : e2));
+                cudaGetErrorString(e0 != cudaSuccess ? e0 : (e1 != cudaSuccess ? e1 : e2)));
   return p->d_err ? vcsr_plan_check(p, stream) : VCSR_OK;
 }
 
