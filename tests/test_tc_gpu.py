@@ -124,6 +124,28 @@ def test_tf32_panels_host_entry_point():
     assert rel_l2(C, ref) <= TOL_TF32
 
 
+def test_tf32_panels_host_pipeline():
+    # 8 MB of B and C: the host entry point runs column chunks of 64 (upload,
+    # product on the plan's compute stream, download), each chunk a TF32 call
+    # on a 64-column slice of the staged B
+    csr = V.gen_csr("blockdense", 2, 4096)
+    O = 256
+    B = V.gen_dense_host(csr.N, O, 6)
+    plan = V.Plan(csr, tf32_panels=True)
+    assert plan.info()["num_panel_blocks"] > 100
+    C = np.empty((csr.M, O), np.float32)
+    plan.spmm_host(B, C)
+    ref = oracle.csr_spmm_f64(csr.M, csr.row_ptr, csr.col, csr.val, B)
+    assert rel_l2(C, ref) <= TOL_TF32
+    dC = torch.empty(csr.M, O, device="cuda")
+    plan.spmm(torch.from_numpy(B).cuda(), dC)
+    plan.check()
+    assert rel_l2(C, dC.cpu().numpy().astype(np.float64)) <= 1e-5
+    C2 = np.empty_like(C)
+    plan.spmm_host(B, C2)
+    assert np.array_equal(C, C2)
+
+
 def test_tf32_panels_need_aligned_o():
     csr = V.gen_csr("blockdense", 0, 1024)
     plan = V.Plan(csr, tf32_panels=True)
