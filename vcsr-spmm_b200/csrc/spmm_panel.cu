@@ -203,6 +203,7 @@ constexpr int min_blocks_for() {
   return VCSR_TUNE_MINB;
 #else
   if (VW == 1) return 1;
+  if (NV == 4) return 2;
   if (R <= 4) return NV == 1 ? 3 : (R == 1 ? 4 : 2);
   if (R == 8) return NV == 1 ? 2 : 1;
   return 2;
@@ -694,6 +695,9 @@ KernelFn pick_r(int NV, int VW, bool is_long, bool rowptr) {
   if constexpr (R == 16) {
     return VW == 4 ? pick_rv<16, 1, 4, TB>(is_long, rowptr) : pick_rv<16, 1, 1, TB>(is_long, rowptr);
   } else {
+    if constexpr (R == 1) {
+      if (NV == 4 && VW == 4) return pick_rv<1, 4, 4, TB>(is_long, rowptr);
+    }
     if (NV == 1)
       return VW == 4 ? pick_rv<R, 1, 4, TB>(is_long, rowptr) : pick_rv<R, 1, 1, TB>(is_long, rowptr);
     return VW == 4 ? pick_rv<R, 2, 4, TB>(is_long, rowptr) : pick_rv<R, 2, 1, TB>(is_long, rowptr);
@@ -751,6 +755,23 @@ LaunchShape pick_shape(int O, int R, bool vec4) {
   while ((1 << s.lshift) < L) ++s.lshift;
   s.W = L * s.VW * s.NV;
   s.n_otiles = (int)ceil_div(O, s.W);
+  return s;
+}
+
+// The vector-panel kernels' shape: pick_shape's, except that single-row
+// vectors at O >= 256 take sub-warps of 16 lanes with four 128-bit columns
+// per lane (twice the B loads in flight per lane; same 256-column tiles).
+// Measured on B200 against 32 lanes x two columns: power-law O=256 403 ->
+// 350 us, uniform O=256 14.5 -> 12.5 us, R-MAT 2^22 O=256 within the run to
+// run spread (6.4-6.7 ms either way).
+static LaunchShape panel_shape(int O, int R, bool vec4) {
+  LaunchShape s = pick_shape(O, R, vec4);
+  if (R == 1 && s.VW == 4 && (int)ceil_div(O, 4) >= 64) {
+    s.lshift = 4;
+    s.NV = 4;
+    s.W = 16 * 4 * 4;
+    s.n_otiles = (int)ceil_div(O, s.W);
+  }
   return s;
 }
 
@@ -830,7 +851,7 @@ vcsr_status launch_panel_spmm(const PanelDevView &P, bool rowptr, const void *B,
   // 128-bit lanes: four B values per load (16 bytes FP32, 8 bytes BF16 / FP16)
   const bool vec4 = (O % 4 == 0) && (ldb % 4 == 0) && (ldc % 4 == 0) &&
                     ((uintptr_t)B % (bt == BType::kF32 ? 16 : 8) == 0) && ((uintptr_t)C % 16 == 0);
-  const LaunchShape s = pick_shape(O, P.R, vec4);
+  const LaunchShape s = panel_shape(O, P.R, vec4);
   if (!rowptr && P.n_split_units > 0 && (O > P.pstride || s.n_otiles > P.counter_stride))
     return fail(VCSR_ERR_INVALID, "O=%d exceeds the plan's max_O=%d", O, P.pstride);
   const int G = 32 >> s.lshift;
