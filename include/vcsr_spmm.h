@@ -306,6 +306,18 @@ vcsr_status vcsr_spmm_host(vcsr_plan *plan, const float *hB, float *hC, int O,
  * the reference (its kernels have no waits). */
 vcsr_status vcsr_plan_check(vcsr_plan *plan, vcsr_stream_t stream);
 
+/* Test hook for the failure path above, not for production use: the next
+ * TF32 panel launch of `plan` withholds one barrier signal in its first block
+ * (the accumulator-ready signal of that block's first item), so the block's
+ * epilogue wait for it runs out after a short bounded poll; the block stops
+ * its other roles, waits for its own copies and MMAs, frees its tensor
+ * memory and records the site, and vcsr_plan_check then returns
+ * VCSR_ERR_TIMEOUT ("accumulator-full ... block 0").  C is incomplete for
+ * that call only; the hook is one-shot.  Nothing faults or hangs.
+ * VCSR_ERR_UNSUPPORTED for a plan without TF32 panels.  No counterpart in the
+ * reference. */
+vcsr_status vcsr_plan_test_withhold_signal(vcsr_plan *plan);
+
 /* ------------------------------------------------------------ peer paths */
 
 /* Race-free SpMM straight on a device VCSR; same contract as

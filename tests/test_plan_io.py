@@ -8,7 +8,9 @@ import struct
 import numpy as np
 import pytest
 
+import oracle
 import vcsr_b200 as V
+from helpers import rel_l2
 
 
 def fnv1a(b: bytes) -> int:
@@ -42,7 +44,7 @@ def test_refuses_other_version_and_bad_header(tmp_path):
         f.write(body + struct.pack("<Q", fnv1a(body)))
     assert load_status(p) == 5
     abi = V.lib().vcsr_abi_version()
-    body = b"VCSRPLAN" + struct.pack("<qq", 2, abi) + struct.pack("<q", -5) + bytes(8 * 34)
+    body = b"VCSRPLAN" + struct.pack("<qq", 3, abi) + struct.pack("<q", -5) + bytes(8 * 34)
     with open(p, "wb") as f:
         f.write(body + struct.pack("<Q", fnv1a(body)))
     assert load_status(p) == 4  # negative M
@@ -79,6 +81,9 @@ def test_round_trip(tmp_path, cfg, size, O, kw):
     b.check()
     t.cuda.synchronize()
     assert t.equal(Ca, Cb)
+    # and the loaded plan's product is the oracle's CSR sum
+    ref = oracle.csr_spmm_f64(csr.M, csr.row_ptr, csr.col, csr.val, B.cpu().numpy())
+    assert rel_l2(Cb.cpu().numpy(), ref) <= (2e-3 if kw.get("tf32_panels") else 1e-5)
     if kw.get("reference_format"):
         ea, eb = a.export(), b.export()
         for f in ("group_ptr", "group_depth", "group_seg_base", "group_rows", "lcol", "val"):

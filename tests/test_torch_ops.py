@@ -5,7 +5,9 @@ from types import SimpleNamespace
 
 import pytest
 
+import oracle
 import vcsr_b200 as V
+from helpers import rel_l2
 
 torch = pytest.importorskip("torch")
 from vcsr_b200 import torch_ops  # noqa: E402
@@ -38,6 +40,8 @@ def test_op_matches_plan():
         plan.spmm(B, C2)
         torch.cuda.synchronize()
         assert torch.equal(C, C2)
+        ref = oracle.csr_spmm_f64(csr.M, csr.row_ptr, csr.col, csr.val, B.cpu().numpy())
+        assert rel_l2(C.cpu().numpy(), ref) <= 1e-5  # the oracle's CSR sum
         Cb = torch.ops.vcsr.spmm(pid, B.to(torch.bfloat16))
         plan.spmm(B.to(torch.bfloat16).float(), C2)
         torch.cuda.synchronize()

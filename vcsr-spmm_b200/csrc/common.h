@@ -3,6 +3,9 @@
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
+#include <exception>
+#include <new>
+#include <stdexcept>
 #include <string>
 
 #include "vcsr_spmm.h"
@@ -15,6 +18,23 @@ vcsr_status fail(vcsr_status s, const char *fmt, ...)
 void clear_error();
 
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Runs an entry point's body and turns a C++ exception of the host code into
+// a status, so that none crosses the C ABI: a host allocation that fails
+// inside a standard container (std::bad_alloc, or std::length_error for a
+// size no container can hold) is VCSR_ERR_ALLOC like a failed malloc.
+template <class F>
+vcsr_status no_throw(F &&body) {
+  try {
+    return body();
+  } catch (const std::bad_alloc &) {
+    return fail(VCSR_ERR_ALLOC, "out of host memory");
+  } catch (const std::length_error &) {
+    return fail(VCSR_ERR_ALLOC, "out of host memory (size beyond a container's limit)");
+  } catch (const std::exception &e) {
+    return fail(VCSR_ERR_INVALID, "host exception: %s", e.what());
+  }
+}
 
 }  // namespace vcsr
 

@@ -46,47 +46,49 @@ vcsr_status vcsr_cusparse_create(int M, int N, int nnz, const int *d_row_ptr,
                                  const int *d_col, const float *d_val,
                                  const float *dB, int O, float *dC, int alg,
                                  vcsr_stream_t stream, vcsr_cusparse **out) {
-  vcsr::clear_error();
-  if (!out) return fail(VCSR_ERR_INVALID, "null out");
-  *out = nullptr;
-  if (M <= 0 || N <= 0 || O <= 0 || nnz < 0)
-    return fail(VCSR_ERR_INVALID, "cuSPARSE harness needs M, N, O > 0");
-  static const cusparseSpMMAlg_t algs[] = {
-      CUSPARSE_SPMM_ALG_DEFAULT, CUSPARSE_SPMM_CSR_ALG1, CUSPARSE_SPMM_CSR_ALG2,
-      CUSPARSE_SPMM_CSR_ALG3};
-  if (alg < 0 || alg > 3) return fail(VCSR_ERR_INVALID, "alg must be 0..3");
-  vcsr_cusparse *x = new vcsr_cusparse();
-  x->alg = algs[alg];
-  VCSR_CUSP(cusparseCreate(&x->h));
-  VCSR_CUSP(cusparseSetStream(x->h, (cudaStream_t)stream));
-  VCSR_CUSP(cusparseCreateCsr(&x->A, M, N, nnz, (void *)d_row_ptr, (void *)d_col,
-                              (void *)d_val, CUSPARSE_INDEX_32I,
-                              CUSPARSE_INDEX_32I, CUSPARSE_INDEX_BASE_ZERO,
-                              CUDA_R_32F));
-  VCSR_CUSP(cusparseCreateDnMat(&x->B, N, O, O, (void *)dB, CUDA_R_32F,
-                                CUSPARSE_ORDER_ROW));
-  VCSR_CUSP(cusparseCreateDnMat(&x->C, M, O, O, (void *)dC, CUDA_R_32F,
-                                CUSPARSE_ORDER_ROW));
-  size_t bytes = 0;
-  VCSR_CUSP(cusparseSpMM_bufferSize(x->h, CUSPARSE_OPERATION_NON_TRANSPOSE,
-                                    CUSPARSE_OPERATION_NON_TRANSPOSE, &x->alpha,
-                                    x->A, x->B, &x->beta, x->C, CUDA_R_32F,
-                                    x->alg, &bytes));
-  if (bytes) {
-    cudaError_t e = cudaMalloc(&x->buf, bytes);
-    if (e != cudaSuccess) {
-      vcsr_cusparse_destroy(x);
-      return fail(VCSR_ERR_ALLOC, "cuSPARSE buffer: %s", cudaGetErrorString(e));
+  return vcsr::no_throw([&]() -> vcsr_status {
+    vcsr::clear_error();
+    if (!out) return fail(VCSR_ERR_INVALID, "null out");
+    *out = nullptr;
+    if (M <= 0 || N <= 0 || O <= 0 || nnz < 0)
+      return fail(VCSR_ERR_INVALID, "cuSPARSE harness needs M, N, O > 0");
+    static const cusparseSpMMAlg_t algs[] = {
+        CUSPARSE_SPMM_ALG_DEFAULT, CUSPARSE_SPMM_CSR_ALG1, CUSPARSE_SPMM_CSR_ALG2,
+        CUSPARSE_SPMM_CSR_ALG3};
+    if (alg < 0 || alg > 3) return fail(VCSR_ERR_INVALID, "alg must be 0..3");
+    vcsr_cusparse *x = new vcsr_cusparse();
+    x->alg = algs[alg];
+    VCSR_CUSP(cusparseCreate(&x->h));
+    VCSR_CUSP(cusparseSetStream(x->h, (cudaStream_t)stream));
+    VCSR_CUSP(cusparseCreateCsr(&x->A, M, N, nnz, (void *)d_row_ptr, (void *)d_col,
+                                (void *)d_val, CUSPARSE_INDEX_32I,
+                                CUSPARSE_INDEX_32I, CUSPARSE_INDEX_BASE_ZERO,
+                                CUDA_R_32F));
+    VCSR_CUSP(cusparseCreateDnMat(&x->B, N, O, O, (void *)dB, CUDA_R_32F,
+                                  CUSPARSE_ORDER_ROW));
+    VCSR_CUSP(cusparseCreateDnMat(&x->C, M, O, O, (void *)dC, CUDA_R_32F,
+                                  CUSPARSE_ORDER_ROW));
+    size_t bytes = 0;
+    VCSR_CUSP(cusparseSpMM_bufferSize(x->h, CUSPARSE_OPERATION_NON_TRANSPOSE,
+                                      CUSPARSE_OPERATION_NON_TRANSPOSE, &x->alpha,
+                                      x->A, x->B, &x->beta, x->C, CUDA_R_32F,
+                                      x->alg, &bytes));
+    if (bytes) {
+      cudaError_t e = cudaMalloc(&x->buf, bytes);
+      if (e != cudaSuccess) {
+        vcsr_cusparse_destroy(x);
+        return fail(VCSR_ERR_ALLOC, "cuSPARSE buffer: %s", cudaGetErrorString(e));
+      }
     }
-  }
-  if (x->alg == CUSPARSE_SPMM_CSR_ALG3) {
-    VCSR_CUSP(cusparseSpMM_preprocess(x->h, CUSPARSE_OPERATION_NON_TRANSPOSE,
-                                      CUSPARSE_OPERATION_NON_TRANSPOSE,
-                                      &x->alpha, x->A, x->B, &x->beta, x->C,
-                                      CUDA_R_32F, x->alg, x->buf));
-  }
-  *out = x;
-  return VCSR_OK;
+    if (x->alg == CUSPARSE_SPMM_CSR_ALG3) {
+      VCSR_CUSP(cusparseSpMM_preprocess(x->h, CUSPARSE_OPERATION_NON_TRANSPOSE,
+                                        CUSPARSE_OPERATION_NON_TRANSPOSE,
+                                        &x->alpha, x->A, x->B, &x->beta, x->C,
+                                        CUDA_R_32F, x->alg, x->buf));
+    }
+    *out = x;
+    return VCSR_OK;
+  });
 }
 
 vcsr_status vcsr_cusparse_run(vcsr_cusparse *x, vcsr_stream_t stream) {

@@ -340,18 +340,20 @@ vcsr_status gen_blockdense(uint64_t seed, int M, vcsr_csr *out) {
 
 extern "C" vcsr_status vcsr_gen_csr(const char *config, uint64_t seed,
                                     int size_param, vcsr_csr *out) {
-  vcsr::clear_error();
-  if (!config || !out) return fail(VCSR_ERR_INVALID, "null argument");
-  std::memset(out, 0, sizeof *out);
-  if (size_param < 0) return fail(VCSR_ERR_INVALID, "negative size_param");
-  std::string c(config);
-  if (c == "uniform") return gen_uniform(seed, size_param ? size_param : 4096, out);
-  if (c == "fem") return gen_fem(seed, size_param ? size_param : 62451, out);
-  if (c == "powerlaw")
-    return gen_powerlaw(seed, size_param ? size_param : 321821, out);
-  if (c == "rmat") return gen_rmat(seed, size_param ? size_param : 22, out);
-  if (c == "blockdense")
-    return gen_blockdense(seed, size_param ? size_param : 65536, out);
-  return fail(VCSR_ERR_INVALID,
-              "unknown config '%s' (uniform|fem|powerlaw|rmat|blockdense)", config);
+  return vcsr::no_throw([&]() -> vcsr_status {
+    vcsr::clear_error();
+    if (!config || !out) return fail(VCSR_ERR_INVALID, "null argument");
+    std::memset(out, 0, sizeof *out);
+    if (size_param < 0) return fail(VCSR_ERR_INVALID, "negative size_param");
+    std::string c(config);
+    if (c == "uniform") return gen_uniform(seed, size_param ? size_param : 4096, out);
+    if (c == "fem") return gen_fem(seed, size_param ? size_param : 62451, out);
+    if (c == "powerlaw")
+      return gen_powerlaw(seed, size_param ? size_param : 321821, out);
+    if (c == "rmat") return gen_rmat(seed, size_param ? size_param : 22, out);
+    if (c == "blockdense")
+      return gen_blockdense(seed, size_param ? size_param : 65536, out);
+    return fail(VCSR_ERR_INVALID,
+                "unknown config '%s' (uniform|fem|powerlaw|rmat|blockdense)", config);
+  });
 }

@@ -117,59 +117,84 @@ extern "C" {
 
 vcsr_status vcsr_mgpu_create(const vcsr_csr *csr, int ngpus, const int *devices,
                              const vcsr_plan_params *params, vcsr_mgpu **out) {
-  vcsr::clear_error();
-  if (!csr || !params || !out || ngpus <= 0) return fail(VCSR_ERR_INVALID, "bad arguments");
-  *out = nullptr;
-  int ndev = 0;
-  VCSR_CUDA(cudaGetDeviceCount(&ndev));
-  auto *m = new vcsr_mgpu();
-  m->n = ngpus;
-  m->M = csr->M; m->N = csr->N; m->nnz = csr->nnz;
-  for (int i = 0; i < ngpus; ++i) {
-    const int d = devices ? devices[i] : i;
-    if (d < 0 || d >= ndev) {
-      delete m;
-      return fail(VCSR_ERR_INVALID, "device %d not visible (%d devices)", d, ndev);
+  return vcsr::no_throw([&]() -> vcsr_status {
+    vcsr::clear_error();
+    if (!csr || !params || !out || ngpus <= 0) return fail(VCSR_ERR_INVALID, "bad arguments");
+    *out = nullptr;
+    int ndev = 0;
+    VCSR_CUDA(cudaGetDeviceCount(&ndev));
+    auto *m = new vcsr_mgpu();
+    m->n = ngpus;
+    m->M = csr->M; m->N = csr->N; m->nnz = csr->nnz;
+    for (int i = 0; i < ngpus; ++i) {
+      const int d = devices ? devices[i] : i;
+      if (d < 0 || d >= ndev) {
+        delete m;
+        return fail(VCSR_ERR_INVALID, "device %d not visible (%d devices)", d, ndev);
+      }
+      m->devs.push_back(d);
     }
-    m->devs.push_back(d);
-  }
-  vcsr_status s = load_nccl(m->nccl);
-  if (s != VCSR_OK) { delete m; return s; }
-  m->cuts.assign(ngpus + 1, 0);
-  s = vcsr_partition_rows(csr->row_ptr, csr->M, ngpus, params->bundle, m->cuts.data());
-  if (s != VCSR_OK) { delete m; return s; }
-  m->plans.assign(ngpus, nullptr);
-  m->streams.assign(ngpus, nullptr);
-  m->ev0.assign(ngpus, nullptr);
-  m->ev1.assign(ngpus, nullptr);
-  m->dB.assign(ngpus, nullptr);
-  m->dC.assign(ngpus, nullptr);
-  m->comms.assign(ngpus, nullptr);
-  for (int i = 0; i < ngpus; ++i) {
-    cudaSetDevice(m->devs[i]);
-    cudaError_t e = cudaStreamCreateWithFlags(&m->streams[i], cudaStreamNonBlocking);
-    if (e == cudaSuccess) e = cudaEventCreate(&m->ev0[i]);
-    if (e == cudaSuccess) e = cudaEventCreate(&m->ev1[i]);
-    if (e != cudaSuccess) {
-      release(m); delete m;
-      return fail(VCSR_ERR_CUDA, "%s", cudaGetErrorString(e));
-    }
-    vcsr_csr panel{};
-    s = vcsr_csr_row_panel(csr, m->cuts[i], m->cuts[i + 1], &panel);
-    if (s == VCSR_OK) s = vcsr_plan_create(&panel, VCSR_HOST, params, &m->plans[i],
-                                           m->streams[i]);
-    vcsr_csr_free(&panel, VCSR_HOST);
-    if (s != VCSR_OK) { release(m); delete m; return s; }
-  }
-  ncclResult_t r = m->nccl.CommInitAll(m->comms.data(), ngpus, m->devs.data());
-  if (r != ncclSuccess) {
+    vcsr_status s = load_nccl(m->nccl);
+    if (s != VCSR_OK) { delete m; return s; }
+    m->cuts.assign(ngpus + 1, 0);
+    s = vcsr_partition_rows(csr->row_ptr, csr->M, ngpus, params->bundle, m->cuts.data());
+    if (s != VCSR_OK) { delete m; return s; }
+    m->plans.assign(ngpus, nullptr);
+    m->streams.assign(ngpus, nullptr);
+    m->ev0.assign(ngpus, nullptr);
+    m->ev1.assign(ngpus, nullptr);
+    m->dB.assign(ngpus, nullptr);
+    m->dC.assign(ngpus, nullptr);
     m->comms.assign(ngpus, nullptr);
-    release(m); delete m;
-    return fail(VCSR_ERR_NCCL, "ncclCommInitAll: %s", m->nccl.GetErrorString(r));
+    for (int i = 0; i < ngpus; ++i) {
+      cudaSetDevice(m->devs[i]);
+      cudaError_t e = cudaStreamCreateWithFlags(&m->streams[i], cudaStreamNonBlocking);
+      if (e == cudaSuccess) e = cudaEventCreate(&m->ev0[i]);
+      if (e == cudaSuccess) e = cudaEventCreate(&m->ev1[i]);
+      if (e != cudaSuccess) {
+        release(m); delete m;
+        return fail(VCSR_ERR_CUDA, "%s", cudaGetErrorString(e));
+      }
+      vcsr_csr panel{};
+      s = vcsr_csr_row_panel(csr, m->cuts[i], m->cuts[i + 1], &panel);
+      if (s == VCSR_OK) s = vcsr_plan_create(&panel, VCSR_HOST, params, &m->plans[i],
+                                             m->streams[i]);
+      vcsr_csr_free(&panel, VCSR_HOST);
+      if (s != VCSR_OK) { release(m); delete m; return s; }
+    }
+    ncclResult_t r = m->nccl.CommInitAll(m->comms.data(), ngpus, m->devs.data());
+    if (r != ncclSuccess) {
+      m->comms.assign(ngpus, nullptr);
+      release(m); delete m;
+      return fail(VCSR_ERR_NCCL, "ncclCommInitAll: %s", m->nccl.GetErrorString(r));
+    }
+    *out = m;
+    return VCSR_OK;
+  });
+}
+
+namespace {
+
+// One grouped broadcast of B (nb floats) from device 0 to every device, each
+// enqueue's result checked: a failed ncclBroadcast ends the group and is
+// reported with NCCL's message.
+vcsr_status broadcast_b(vcsr_mgpu *m, size_t nb) {
+  ncclResult_t r = m->nccl.GroupStart();
+  if (r != ncclSuccess) return fail(VCSR_ERR_NCCL, "ncclGroupStart: %s", m->nccl.GetErrorString(r));
+  for (int i = 0; i < m->n; ++i) {
+    cudaSetDevice(m->devs[i]);
+    r = m->nccl.Broadcast(m->dB[i], m->dB[i], nb, ncclFloat, 0, m->comms[i], m->streams[i]);
+    if (r != ncclSuccess) {
+      m->nccl.GroupEnd();
+      return fail(VCSR_ERR_NCCL, "ncclBroadcast: %s", m->nccl.GetErrorString(r));
+    }
   }
-  *out = m;
+  r = m->nccl.GroupEnd();
+  if (r != ncclSuccess) return fail(VCSR_ERR_NCCL, "ncclGroupEnd: %s", m->nccl.GetErrorString(r));
   return VCSR_OK;
 }
+
+}  // namespace
 
 vcsr_status vcsr_mgpu_set_b(vcsr_mgpu *m, const float *hB, int O, float *bcast_ms) {
   vcsr::clear_error();
@@ -190,29 +215,13 @@ vcsr_status vcsr_mgpu_set_b(vcsr_mgpu *m, const float *hB, int O, float *bcast_m
                             m->streams[0]));
   VCSR_CUDA(cudaStreamSynchronize(m->streams[0]));
   // the first broadcast on a buffer carries NCCL's set-up; run it untimed
-  m->nccl.GroupStart();
-  for (int i = 0; i < m->n; ++i) {
-    cudaSetDevice(m->devs[i]);
-    m->nccl.Broadcast(m->dB[i], m->dB[i], nb, ncclFloat, 0, m->comms[i], m->streams[i]);
-  }
-  if (m->nccl.GroupEnd() != ncclSuccess) return fail(VCSR_ERR_NCCL, "ncclGroupEnd failed");
+  VCSR_TRY(broadcast_b(m, nb));
   VCSR_TRY(wait_all(m, true));
   for (int i = 0; i < m->n; ++i) {
     cudaSetDevice(m->devs[i]);
     VCSR_CUDA(cudaEventRecord(m->ev0[i], m->streams[i]));
   }
-  m->nccl.GroupStart();
-  for (int i = 0; i < m->n; ++i) {
-    cudaSetDevice(m->devs[i]);
-    ncclResult_t r = m->nccl.Broadcast(m->dB[i], m->dB[i], nb, ncclFloat, 0, m->comms[i],
-                                       m->streams[i]);
-    if (r != ncclSuccess) {
-      m->nccl.GroupEnd();
-      return fail(VCSR_ERR_NCCL, "ncclBroadcast: %s", m->nccl.GetErrorString(r));
-    }
-  }
-  ncclResult_t r = m->nccl.GroupEnd();
-  if (r != ncclSuccess) return fail(VCSR_ERR_NCCL, "ncclGroupEnd: %s", m->nccl.GetErrorString(r));
+  VCSR_TRY(broadcast_b(m, nb));
   for (int i = 0; i < m->n; ++i) {
     cudaSetDevice(m->devs[i]);
     VCSR_CUDA(cudaEventRecord(m->ev1[i], m->streams[i]));

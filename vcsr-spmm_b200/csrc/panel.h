@@ -48,6 +48,7 @@ struct PanelHost {
   std::vector<int> vec_ptr;  // num_vectors + 1 offsets into ucol
   std::vector<int> ucol;     // union column per entry
   std::vector<float> uval;   // R values per entry
+  std::vector<uint32_t> umask;  // R > 1: bit r = row r holds the entry (else padding)
   std::vector<Unit> units;
   std::vector<SplitPart> parts;
   std::vector<SplitVec> svecs;

@@ -111,6 +111,7 @@ vcsr_status build_panel_host(const vcsr_csr &csr, int R, int chunk, int sms,
     for (int v = 0; v <= V; ++v) out->vec_ptr[v] = (int)cnt[v];
     out->ucol.assign((size_t)cnt[V], 0);
     out->uval.assign((size_t)cnt[V] * R, 0.f);
+    out->umask.assign((size_t)cnt[V], 0u);
 #pragma omp parallel
     {
       std::vector<uint64_t> k;
@@ -129,6 +130,7 @@ vcsr_status build_panel_host(const vcsr_csr &csr, int R, int chunk, int sms,
             const uint64_t key = ((uint64_t)(uint32_t)csr.col[p] << 32) | (uint32_t)occ;
             while (k[j] < key) ++j;
             out->uval[(size_t)(base + j) * R + (r - r0)] = csr.val[p];
+            out->umask[(size_t)(base + j)] |= 1u << (r - r0);
           }
         }
       }

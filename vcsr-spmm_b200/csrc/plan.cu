@@ -25,7 +25,7 @@ using vcsr::upload;
 namespace vcsr {
 
 void plan_release(vcsr_plan *p) {
-  cudaFree(p->d_ucol); cudaFree(p->d_uval); cudaFree(p->d_units);
+  cudaFree(p->d_ucol); cudaFree(p->d_uval); cudaFree(p->d_umask); cudaFree(p->d_units);
   cudaFree(p->d_batches); cudaFree(p->d_long); cudaFree(p->d_vec_ptr);
   cudaFree(p->d_parts); cudaFree(p->d_svecs); cudaFree(p->d_partials);
   cudaFree(p->d_counters); cudaFree(p->d_stage_B); cudaFree(p->d_stage_C);
@@ -67,6 +67,7 @@ vcsr::PanelDevView view(const vcsr_plan *p) {
   vcsr::PanelDevView v;
   v.ucol = p->d_ucol;
   v.uval = p->d_uval;
+  v.umask = p->R > 1 ? p->d_umask : nullptr;
   v.units = p->d_units;
   v.n_units = p->n_units;
   v.batches = p->d_batches;
@@ -181,241 +182,244 @@ void vcsr_plan_params_default(vcsr_plan_params *p) {
 vcsr_status vcsr_plan_create(const vcsr_csr *csr, int csr_where,
                              const vcsr_plan_params *params, vcsr_plan **out,
                              vcsr_stream_t stream) {
-  vcsr::clear_error();
-  if (!csr || !params || !out) return fail(VCSR_ERR_INVALID, "null argument");
-  *out = nullptr;
-  if (csr->M < 0 || csr->N < 0 || csr->nnz < 0)
-    return fail(VCSR_ERR_INVALID, "negative matrix size");
-  if (params->segw <= 0 || params->bundle <= 0)
-    return fail(VCSR_ERR_INVALID, "segw and bundle must be > 0");
-  if (params->max_O < 0 || params->tileK < 0)
-    return fail(VCSR_ERR_INVALID, "negative max_O or tileK");
-  if (csr->M > 0 && !csr->row_ptr) return fail(VCSR_ERR_INVALID, "null row_ptr");
-  if (csr->nnz > 0 && (!csr->col || !csr->val))
-    return fail(VCSR_ERR_INVALID, "null col/val");
-  const auto t0 = std::chrono::steady_clock::now();
-  cudaStream_t st = (cudaStream_t)stream;
-  vcsr_plan *p = new (std::nothrow) vcsr_plan();
-  if (!p) return fail(VCSR_ERR_ALLOC, "out of host memory");
-  p->M = csr->M; p->N = csr->N; p->nnz = csr->nnz;
-  p->params = *params;
-  cudaGetDevice(&p->device);
-  int sms = 148;
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, p->device);
+  return vcsr::no_throw([&]() -> vcsr_status {
+    vcsr::clear_error();
+    if (!csr || !params || !out) return fail(VCSR_ERR_INVALID, "null argument");
+    *out = nullptr;
+    if (csr->M < 0 || csr->N < 0 || csr->nnz < 0)
+      return fail(VCSR_ERR_INVALID, "negative matrix size");
+    if (params->segw <= 0 || params->bundle <= 0)
+      return fail(VCSR_ERR_INVALID, "segw and bundle must be > 0");
+    if (params->max_O < 0 || params->tileK < 0)
+      return fail(VCSR_ERR_INVALID, "negative max_O or tileK");
+    if (csr->M > 0 && !csr->row_ptr) return fail(VCSR_ERR_INVALID, "null row_ptr");
+    if (csr->nnz > 0 && (!csr->col || !csr->val))
+      return fail(VCSR_ERR_INVALID, "null col/val");
+    const auto t0 = std::chrono::steady_clock::now();
+    cudaStream_t st = (cudaStream_t)stream;
+    vcsr_plan *p = new (std::nothrow) vcsr_plan();
+    if (!p) return fail(VCSR_ERR_ALLOC, "out of host memory");
+    p->M = csr->M; p->N = csr->N; p->nnz = csr->nnz;
+    p->params = *params;
+    cudaGetDevice(&p->device);
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, p->device);
 
-  vcsr_csr h{};
-  bool owned = false;
-  vcsr_csr empty_rp{};
-  std::vector<int> zero_rp;
-  if (csr->M == 0) {  // nothing to read; keep a valid row_ptr
-    zero_rp.assign(1, 0);
-    empty_rp = *csr;
-    empty_rp.row_ptr = zero_rp.data();
-    h = empty_rp;
-  } else {
-    vcsr_status s = host_sorted_csr(csr, csr_where, &h, &owned);
-    if (s != VCSR_OK) { delete p; return s; }
-  }
+    vcsr_csr h{};
+    bool owned = false;
+    vcsr_csr empty_rp{};
+    std::vector<int> zero_rp;
+    if (csr->M == 0) {  // nothing to read; keep a valid row_ptr
+      zero_rp.assign(1, 0);
+      empty_rp = *csr;
+      empty_rp.row_ptr = zero_rp.data();
+      h = empty_rp;
+    } else {
+      vcsr_status s = host_sorted_csr(csr, csr_where, &h, &owned);
+      if (s != VCSR_OK) { delete p; return s; }
+    }
 
-  // TF32 panels: the dense 16x16 blocks go to the tensor-core path, the
-  // rest (the residual) to the row-stationary layout below
-  vcsr::TcHost tc;
-  std::vector<int> r_rp, r_col;
-  std::vector<float> r_val;
-  vcsr_csr work = h;
-  if ((params->flags & VCSR_PLAN_TF32_PANELS) && h.M > 0) {
-    if (params->panel_min_nnz < 0 || params->panel_min_nnz > 256) {
-      if (owned) vcsr_csr_free(&h, VCSR_HOST);
-      delete p;
-      return fail(VCSR_ERR_INVALID, "panel_min_nnz must be in [0, 256]");
-    }
-    const int min_nnz = params->panel_min_nnz > 0 ? params->panel_min_nnz : 128;
-    vcsr_status s0 = vcsr::split_dense_panels(h, min_nnz, &tc, r_rp, r_col, r_val);
-    if (s0 != VCSR_OK) {
-      if (owned) vcsr_csr_free(&h, VCSR_HOST);
-      delete p;
-      return s0;
-    }
-    work.nnz = r_rp.back();
-    work.row_ptr = r_rp.data();
-    work.col = r_col.data();
-    work.val = r_val.data();
-    p->n_panel_rb = (int)tc.rb_row.size();
-    p->n_panel_blocks = (int)tc.blk_col.size();
-    p->panel_nnz = (int64_t)h.nnz - work.nnz;
-  }
-  vcsr::PanelHost ph;
-  int R = params->vec_rows;
-  if (R == 0) {
-    R = vcsr::choose_vec_rows(work, nullptr);
-    if (R == 8 && params->target_O > 128) R = 4;
-  }
-  vcsr_status s = vcsr::build_panel_host(work, R, params->chunk, sms, &ph);
-  if (s != VCSR_OK) {
-    if (owned) vcsr_csr_free(&h, VCSR_HOST);
-    delete p;
-    return s;
-  }
-  p->R = ph.R;
-  p->num_vectors = ph.num_vectors;
-  p->num_union = (int64_t)ph.ucol.size();
-  p->chunk = ph.chunk;
-  p->n_units = (int)ph.units.size();
-  p->n_split_units = (int)ph.parts.size();
-  p->n_split_vectors = (int)ph.svecs.size();
-  p->pstride = std::max(params->max_O, 1);
-  p->counter_stride = std::max(params->max_O, 1);
-  static_assert(sizeof(vcsr::Unit) == sizeof(int4), "Unit must match int4");
-  static_assert(sizeof(vcsr::SplitPart) == sizeof(int2), "SplitPart must match int2");
-  static_assert(sizeof(vcsr::SplitVec) == sizeof(int2), "SplitVec must match int2");
-  std::vector<int4> units(ph.units.size());
-  std::memcpy(units.data(), ph.units.data(), sizeof(int4) * units.size());
-  // Split parts and units of at least kLongUnit union columns are walked by a
-  // whole warp (its sub-warps split the columns).  The other vectors are
-  // packed, in order, into batches of consecutive vectors walked by one
-  // sub-warp each; a batch holds at most 64 vectors and about `batch_cols`
-  // union columns, chosen so that there are ~64 batches per SM.  With R > 2
-  // a batch is one vector (vectors are long enough on their own).
-  constexpr int kLongUnit = 128, kMaxBatchVecs = 64;
-  std::vector<int> long_idx;
-  std::vector<int4> batches;
-  int64_t short_cols = 0;
-  for (const auto &u : ph.units)
-    if (u.slot < 0 && u.end - u.begin < kLongUnit) short_cols += u.end - u.begin;
-  const int64_t batch_cols =
-      std::max<int64_t>(16, std::min<int64_t>(256, short_cols / ((int64_t)sms * 64)));
-  {
-    int4 cur = make_int4(-1, -1, 0, 0);
-    auto close = [&]() {
-      if (cur.x >= 0) batches.push_back(cur);
-      cur.x = -1;
-    };
-    for (size_t u = 0; u < ph.units.size(); ++u) {
-      const auto &un = ph.units[u];
-      const int len = un.end - un.begin;
-      if (un.slot >= 0 || len >= kLongUnit) {
-        long_idx.push_back((int)u);
-        close();
-        continue;
+    // TF32 panels: the dense 16x16 blocks go to the tensor-core path, the
+    // rest (the residual) to the row-stationary layout below
+    vcsr::TcHost tc;
+    std::vector<int> r_rp, r_col;
+    std::vector<float> r_val;
+    vcsr_csr work = h;
+    if ((params->flags & VCSR_PLAN_TF32_PANELS) && h.M > 0) {
+      if (params->panel_min_nnz < 0 || params->panel_min_nnz > 256) {
+        if (owned) vcsr_csr_free(&h, VCSR_HOST);
+        delete p;
+        return fail(VCSR_ERR_INVALID, "panel_min_nnz must be in [0, 256]");
       }
-      if (cur.x >= 0 && (ph.R > 2 || cur.w - cur.z + len > batch_cols ||
-                         cur.y - cur.x >= kMaxBatchVecs))
-        close();
-      if (cur.x < 0) cur = make_int4(un.vec, un.vec, un.begin, un.begin);
-      cur.y = un.vec + 1;
-      cur.w = un.end;
+      const int min_nnz = params->panel_min_nnz > 0 ? params->panel_min_nnz : 128;
+      vcsr_status s0 = vcsr::split_dense_panels(h, min_nnz, &tc, r_rp, r_col, r_val);
+      if (s0 != VCSR_OK) {
+        if (owned) vcsr_csr_free(&h, VCSR_HOST);
+        delete p;
+        return s0;
+      }
+      work.nnz = r_rp.back();
+      work.row_ptr = r_rp.data();
+      work.col = r_col.data();
+      work.val = r_val.data();
+      p->n_panel_rb = (int)tc.rb_row.size();
+      p->n_panel_blocks = (int)tc.blk_col.size();
+      p->panel_nnz = (int64_t)h.nnz - work.nnz;
     }
-    close();
-  }
-  p->n_batches = (int)batches.size();
-  p->n_long = (int)long_idx.size();
-  // Row panels (cut at vectors where a batch or a long unit starts) for the
-  // host entry point's row pipeline; not with TF32 panels, whose kernel
-  // covers all rows at once.  Cuts at 1/32, 1/6, ..., 5/6 and 31/32 of the
-  // entries: the small first and last panels shorten the pipeline's fill
-  // (the first upload before any product) and drain (the last download
-  // after the last upload); measured on FEM at O = 32 / 128 / 512 against
-  // eight equal panels: -16% / -2% / -1% per call (more panels cost more
-  // per-panel overhead than they save).
-  if (p->n_panel_rb == 0 && work.M >= 8192 && work.nnz >= (1 << 20)) {
-    constexpr int kRowPanels = 8;
-    constexpr double kCut[kRowPanels - 1] = {1.0 / 32, 1.0 / 6, 2.0 / 6, 3.0 / 6,
-                                             4.0 / 6,  5.0 / 6, 31.0 / 32};
-    std::vector<int> cuts;  // vector indices where a panel may start
-    for (const int4 &b : batches) cuts.push_back(b.x);
-    for (int u : long_idx) cuts.push_back(ph.units[u].vec);
-    std::sort(cuts.begin(), cuts.end());
-    cuts.erase(std::unique(cuts.begin(), cuts.end()), cuts.end());
-    std::vector<int> vb{0};
-    for (int j = 1; j < kRowPanels; ++j) {
-      const int64_t target = (int64_t)(work.nnz * kCut[j - 1]);
-      const int row = (int)(std::lower_bound(work.row_ptr, work.row_ptr + work.M + 1, target) -
-                            work.row_ptr);
-      auto it = std::lower_bound(cuts.begin(), cuts.end(), row / ph.R);
-      if (it != cuts.end() && *it > vb.back()) vb.push_back(*it);
+    vcsr::PanelHost ph;
+    int R = params->vec_rows;
+    if (R == 0) {
+      R = vcsr::choose_vec_rows(work, nullptr);
+      if (R == 8 && params->target_O > 128) R = 4;
     }
-    vb.push_back(ph.num_vectors);
-    std::vector<int> lvec(long_idx.size());
-    for (size_t i = 0; i < long_idx.size(); ++i) lvec[i] = ph.units[long_idx[i]].vec;
-    std::vector<int> bvec(batches.size());
-    for (size_t i = 0; i < batches.size(); ++i) bvec[i] = batches[i].x;
-    for (size_t j = 0; j + 1 < vb.size(); ++j) {
-      vcsr_plan::RowPanel rp;
-      rp.row0 = vb[j] * ph.R;
-      rp.row1 = std::min(work.M, vb[j + 1] * ph.R);
-      rp.b0 = (int)(std::lower_bound(bvec.begin(), bvec.end(), vb[j]) - bvec.begin());
-      rp.b1 = (int)(std::lower_bound(bvec.begin(), bvec.end(), vb[j + 1]) - bvec.begin());
-      rp.l0 = (int)(std::lower_bound(lvec.begin(), lvec.end(), vb[j]) - lvec.begin());
-      rp.l1 = (int)(std::lower_bound(lvec.begin(), lvec.end(), vb[j + 1]) - lvec.begin());
-      rp.col_max = -1;
-      for (int r = rp.row0; r < rp.row1; ++r)
-        if (work.row_ptr[r + 1] > work.row_ptr[r])
-          rp.col_max = std::max(rp.col_max, work.col[work.row_ptr[r + 1] - 1]);
-      p->rpanels.push_back(rp);
-    }
-  }
-  std::vector<int2> parts(ph.parts.size()), svecs(ph.svecs.size());
-  std::memcpy(parts.data(), ph.parts.data(), sizeof(int2) * parts.size());
-  std::memcpy(svecs.data(), ph.svecs.data(), sizeof(int2) * svecs.size());
-  if ((s = upload(&p->d_ucol, ph.ucol, st, &p->panel_bytes)) ||
-      (s = upload(&p->d_uval, ph.uval, st, &p->panel_bytes)) ||
-      (s = upload(&p->d_units, units, st, &p->panel_bytes)) ||
-      (s = upload(&p->d_parts, parts, st, &p->panel_bytes)) ||
-      (s = upload(&p->d_svecs, svecs, st, &p->panel_bytes)) ||
-      (s = upload(&p->d_batches, batches, st, &p->panel_bytes)) ||
-      (s = upload(&p->d_long, long_idx, st, &p->panel_bytes)) ||
-      (s = upload(&p->d_vec_ptr, ph.vec_ptr, st, &p->panel_bytes))) {
-    if (owned) vcsr_csr_free(&h, VCSR_HOST);
-    vcsr::plan_release(p);
-    delete p;
-    return s;
-  }
-  if (p->n_panel_rb > 0) {
-    std::vector<int> zero1(1, 0);
-    if ((s = upload(&p->d_rb_row, tc.rb_row, st, &p->panel_bytes)) ||
-        (s = upload(&p->d_rb_ptr, tc.rb_ptr, st, &p->panel_bytes)) ||
-        (s = upload(&p->d_blk_col, tc.blk_col, st, &p->panel_bytes)) ||
-        (s = upload(&p->d_blk_val, tc.blk_val, st, &p->panel_bytes)) ||
-        (s = upload(&p->d_err, zero1, st, &p->panel_bytes))) {
-      if (owned) vcsr_csr_free(&h, VCSR_HOST);
-      vcsr::plan_release(p);
-      delete p;
-      return s;
-    }
-  }
-  if ((s = vcsr::plan_finish(p, st)) != VCSR_OK) {
-    if (owned) vcsr_csr_free(&h, VCSR_HOST);
-    vcsr::plan_release(p);
-    delete p;
-    return s;
-  }
-  if (params->flags & VCSR_PLAN_REFERENCE_FORMAT) {
-    vcsr_csr d{};
-    s = vcsr_csr_to_device(&h, &d, stream);
-    if (s == VCSR_OK) s = vcsr_build_vcsr(&d, params->segw, params->bundle, &p->ref, stream);
-    if (d.row_ptr) {
-      cudaStreamSynchronize(st);
-      vcsr_csr_free(&d, VCSR_DEVICE);
-    }
+    vcsr_status s = vcsr::build_panel_host(work, R, params->chunk, sms, &ph);
     if (s != VCSR_OK) {
       if (owned) vcsr_csr_free(&h, VCSR_HOST);
+      delete p;
+      return s;
+    }
+    p->R = ph.R;
+    p->num_vectors = ph.num_vectors;
+    p->num_union = (int64_t)ph.ucol.size();
+    p->chunk = ph.chunk;
+    p->n_units = (int)ph.units.size();
+    p->n_split_units = (int)ph.parts.size();
+    p->n_split_vectors = (int)ph.svecs.size();
+    p->pstride = std::max(params->max_O, 1);
+    p->counter_stride = std::max(params->max_O, 1);
+    static_assert(sizeof(vcsr::Unit) == sizeof(int4), "Unit must match int4");
+    static_assert(sizeof(vcsr::SplitPart) == sizeof(int2), "SplitPart must match int2");
+    static_assert(sizeof(vcsr::SplitVec) == sizeof(int2), "SplitVec must match int2");
+    std::vector<int4> units(ph.units.size());
+    std::memcpy(units.data(), ph.units.data(), sizeof(int4) * units.size());
+    // Split parts and units of at least kLongUnit union columns are walked by a
+    // whole warp (its sub-warps split the columns).  The other vectors are
+    // packed, in order, into batches of consecutive vectors walked by one
+    // sub-warp each; a batch holds at most 64 vectors and about `batch_cols`
+    // union columns, chosen so that there are ~64 batches per SM.  With R > 2
+    // a batch is one vector (vectors are long enough on their own).
+    constexpr int kLongUnit = 128, kMaxBatchVecs = 64;
+    std::vector<int> long_idx;
+    std::vector<int4> batches;
+    int64_t short_cols = 0;
+    for (const auto &u : ph.units)
+      if (u.slot < 0 && u.end - u.begin < kLongUnit) short_cols += u.end - u.begin;
+    const int64_t batch_cols =
+        std::max<int64_t>(16, std::min<int64_t>(256, short_cols / ((int64_t)sms * 64)));
+    {
+      int4 cur = make_int4(-1, -1, 0, 0);
+      auto close = [&]() {
+        if (cur.x >= 0) batches.push_back(cur);
+        cur.x = -1;
+      };
+      for (size_t u = 0; u < ph.units.size(); ++u) {
+        const auto &un = ph.units[u];
+        const int len = un.end - un.begin;
+        if (un.slot >= 0 || len >= kLongUnit) {
+          long_idx.push_back((int)u);
+          close();
+          continue;
+        }
+        if (cur.x >= 0 && (ph.R > 2 || cur.w - cur.z + len > batch_cols ||
+                           cur.y - cur.x >= kMaxBatchVecs))
+          close();
+        if (cur.x < 0) cur = make_int4(un.vec, un.vec, un.begin, un.begin);
+        cur.y = un.vec + 1;
+        cur.w = un.end;
+      }
+      close();
+    }
+    p->n_batches = (int)batches.size();
+    p->n_long = (int)long_idx.size();
+    // Row panels (cut at vectors where a batch or a long unit starts) for the
+    // host entry point's row pipeline; not with TF32 panels, whose kernel
+    // covers all rows at once.  Cuts at 1/32, 1/6, ..., 5/6 and 31/32 of the
+    // entries: the small first and last panels shorten the pipeline's fill
+    // (the first upload before any product) and drain (the last download
+    // after the last upload); measured on FEM at O = 32 / 128 / 512 against
+    // eight equal panels: -16% / -2% / -1% per call (more panels cost more
+    // per-panel overhead than they save).
+    if (p->n_panel_rb == 0 && work.M >= 8192 && work.nnz >= (1 << 20)) {
+      constexpr int kRowPanels = 8;
+      constexpr double kCut[kRowPanels - 1] = {1.0 / 32, 1.0 / 6, 2.0 / 6, 3.0 / 6,
+                                               4.0 / 6,  5.0 / 6, 31.0 / 32};
+      std::vector<int> cuts;  // vector indices where a panel may start
+      for (const int4 &b : batches) cuts.push_back(b.x);
+      for (int u : long_idx) cuts.push_back(ph.units[u].vec);
+      std::sort(cuts.begin(), cuts.end());
+      cuts.erase(std::unique(cuts.begin(), cuts.end()), cuts.end());
+      std::vector<int> vb{0};
+      for (int j = 1; j < kRowPanels; ++j) {
+        const int64_t target = (int64_t)(work.nnz * kCut[j - 1]);
+        const int row = (int)(std::lower_bound(work.row_ptr, work.row_ptr + work.M + 1, target) -
+                              work.row_ptr);
+        auto it = std::lower_bound(cuts.begin(), cuts.end(), row / ph.R);
+        if (it != cuts.end() && *it > vb.back()) vb.push_back(*it);
+      }
+      vb.push_back(ph.num_vectors);
+      std::vector<int> lvec(long_idx.size());
+      for (size_t i = 0; i < long_idx.size(); ++i) lvec[i] = ph.units[long_idx[i]].vec;
+      std::vector<int> bvec(batches.size());
+      for (size_t i = 0; i < batches.size(); ++i) bvec[i] = batches[i].x;
+      for (size_t j = 0; j + 1 < vb.size(); ++j) {
+        vcsr_plan::RowPanel rp;
+        rp.row0 = vb[j] * ph.R;
+        rp.row1 = std::min(work.M, vb[j + 1] * ph.R);
+        rp.b0 = (int)(std::lower_bound(bvec.begin(), bvec.end(), vb[j]) - bvec.begin());
+        rp.b1 = (int)(std::lower_bound(bvec.begin(), bvec.end(), vb[j + 1]) - bvec.begin());
+        rp.l0 = (int)(std::lower_bound(lvec.begin(), lvec.end(), vb[j]) - lvec.begin());
+        rp.l1 = (int)(std::lower_bound(lvec.begin(), lvec.end(), vb[j + 1]) - lvec.begin());
+        rp.col_max = -1;
+        for (int r = rp.row0; r < rp.row1; ++r)
+          if (work.row_ptr[r + 1] > work.row_ptr[r])
+            rp.col_max = std::max(rp.col_max, work.col[work.row_ptr[r + 1] - 1]);
+        p->rpanels.push_back(rp);
+      }
+    }
+    std::vector<int2> parts(ph.parts.size()), svecs(ph.svecs.size());
+    std::memcpy(parts.data(), ph.parts.data(), sizeof(int2) * parts.size());
+    std::memcpy(svecs.data(), ph.svecs.data(), sizeof(int2) * svecs.size());
+    if ((s = upload(&p->d_ucol, ph.ucol, st, &p->panel_bytes)) ||
+        (s = upload(&p->d_uval, ph.uval, st, &p->panel_bytes)) ||
+        (s = upload(&p->d_umask, ph.umask, st, &p->panel_bytes)) ||
+        (s = upload(&p->d_units, units, st, &p->panel_bytes)) ||
+        (s = upload(&p->d_parts, parts, st, &p->panel_bytes)) ||
+        (s = upload(&p->d_svecs, svecs, st, &p->panel_bytes)) ||
+        (s = upload(&p->d_batches, batches, st, &p->panel_bytes)) ||
+        (s = upload(&p->d_long, long_idx, st, &p->panel_bytes)) ||
+        (s = upload(&p->d_vec_ptr, ph.vec_ptr, st, &p->panel_bytes))) {
+      if (owned) vcsr_csr_free(&h, VCSR_HOST);
       vcsr::plan_release(p);
       delete p;
       return s;
     }
-    p->has_ref = true;
-  }
-  cudaError_t e = cudaStreamSynchronize(st);  // host vectors die here
-  if (owned) vcsr_csr_free(&h, VCSR_HOST);
-  if (e != cudaSuccess) {
-    vcsr::plan_release(p);
-    delete p;
-    return fail(VCSR_ERR_CUDA, "plan upload: %s", cudaGetErrorString(e));
-  }
-  p->build_ms = std::chrono::duration<double, std::milli>(
-                    std::chrono::steady_clock::now() - t0).count();
-  *out = p;
-  return VCSR_OK;
+    if (p->n_panel_rb > 0) {
+      std::vector<int> zero1(1, 0);
+      if ((s = upload(&p->d_rb_row, tc.rb_row, st, &p->panel_bytes)) ||
+          (s = upload(&p->d_rb_ptr, tc.rb_ptr, st, &p->panel_bytes)) ||
+          (s = upload(&p->d_blk_col, tc.blk_col, st, &p->panel_bytes)) ||
+          (s = upload(&p->d_blk_val, tc.blk_val, st, &p->panel_bytes)) ||
+          (s = upload(&p->d_err, zero1, st, &p->panel_bytes))) {
+        if (owned) vcsr_csr_free(&h, VCSR_HOST);
+        vcsr::plan_release(p);
+        delete p;
+        return s;
+      }
+    }
+    if ((s = vcsr::plan_finish(p, st)) != VCSR_OK) {
+      if (owned) vcsr_csr_free(&h, VCSR_HOST);
+      vcsr::plan_release(p);
+      delete p;
+      return s;
+    }
+    if (params->flags & VCSR_PLAN_REFERENCE_FORMAT) {
+      vcsr_csr d{};
+      s = vcsr_csr_to_device(&h, &d, stream);
+      if (s == VCSR_OK) s = vcsr_build_vcsr(&d, params->segw, params->bundle, &p->ref, stream);
+      if (d.row_ptr) {
+        cudaStreamSynchronize(st);
+        vcsr_csr_free(&d, VCSR_DEVICE);
+      }
+      if (s != VCSR_OK) {
+        if (owned) vcsr_csr_free(&h, VCSR_HOST);
+        vcsr::plan_release(p);
+        delete p;
+        return s;
+      }
+      p->has_ref = true;
+    }
+    cudaError_t e = cudaStreamSynchronize(st);  // host vectors die here
+    if (owned) vcsr_csr_free(&h, VCSR_HOST);
+    if (e != cudaSuccess) {
+      vcsr::plan_release(p);
+      delete p;
+      return fail(VCSR_ERR_CUDA, "plan upload: %s", cudaGetErrorString(e));
+    }
+    p->build_ms = std::chrono::duration<double, std::milli>(
+                      std::chrono::steady_clock::now() - t0).count();
+    *out = p;
+    return VCSR_OK;
+  });
 }
 
 vcsr_status vcsr_plan_get_info(const vcsr_plan *p, vcsr_plan_info *info) {
@@ -479,6 +483,7 @@ vcsr_status vcsr_spmm(const vcsr_plan *p, const float *dB, int ldb, float *dC,
     tv.blk_val = p->d_blk_val;
     tv.M = p->M;
     tv.err = p->d_err;
+    tv.inject = p->tc_inject.exchange(0);
     VCSR_TRY(vcsr::launch_tc_panels(tv, dB, p->N, ldb, dC, ldc, O, (cudaStream_t)stream, &n2));
   }
   if (launches) *launches = n1 + n2;
@@ -563,163 +568,174 @@ vcsr_status vcsr_spmm_f16(const vcsr_plan *p, const void *dB, int ldb, float *dC
 
 vcsr_status vcsr_spmm_host(vcsr_plan *p, const float *hB, float *hC, int O,
                            vcsr_stream_t stream) {
-  vcsr::clear_error();
-  if (!p || !hC || (!hB && p->N > 0 && O > 0))
-    return fail(VCSR_ERR_INVALID, "null argument");
-  if (O < 0) return fail(VCSR_ERR_INVALID, "negative O");
-  cudaStream_t st = (cudaStream_t)stream;
-  const size_t nb = sizeof(float) * (size_t)p->N * O;
-  const size_t nc = sizeof(float) * (size_t)p->M * O;
-  if (nb > p->stage_B) {
-    cudaFree(p->d_stage_B);
-    p->d_stage_B = nullptr;
-    p->stage_B = 0;
-    VCSR_CUDA(cudaMalloc(&p->d_stage_B, nb));
-    p->stage_B = nb;
-  }
-  if (nc > p->stage_C) {
-    cudaFree(p->d_stage_C);
-    p->d_stage_C = nullptr;
-    p->stage_C = 0;
-    VCSR_CUDA(cudaMalloc(&p->d_stage_C, nc));
-    p->stage_C = nc;
-  }
-  constexpr size_t kPipelineBytes = (size_t)8 << 20;
-  if (O > 0 && p->N > 0 && p->M > 0 && nb + nc >= kPipelineBytes && !p->rpanels.empty() &&
-      !(p->n_split_units > 0 && O > p->pstride)) {
-    // Row pipeline for banded matrices: B goes up in P contiguous row chunks
-    // on `stream`, chunk j ending at the highest column that row panels
-    // 0..j read (the last one at N); row panel j runs on the plan's compute
-    // stream as soon as chunk j is up, and its C rows go back on the
-    // download stream.  Used when no panel reads B rows beyond the next
-    // equal 1/P share of B, so that the chunks stay balanced and uploads,
-    // products and downloads overlap.
-    const int P = (int)p->rpanels.size();
-    const int per = (p->N + P - 1) / P;
-    bool banded = true;
-    std::vector<int> cend(P);
-    for (int j = 0, c = 0; j < P; ++j) {
-      const int cm = p->rpanels[j].col_max;
-      if (j + 1 < P && cm >= 0 && cm / per > j + 1) banded = false;
-      c = std::max(c, std::min(p->N, cm + 1));
-      cend[j] = j == P - 1 ? p->N : c;
+  return vcsr::no_throw([&]() -> vcsr_status {
+    vcsr::clear_error();
+    if (!p || !hC || (!hB && p->N > 0 && O > 0))
+      return fail(VCSR_ERR_INVALID, "null argument");
+    if (O < 0) return fail(VCSR_ERR_INVALID, "negative O");
+    cudaStream_t st = (cudaStream_t)stream;
+    const size_t nb = sizeof(float) * (size_t)p->N * O;
+    const size_t nc = sizeof(float) * (size_t)p->M * O;
+    if (nb > p->stage_B) {
+      cudaFree(p->d_stage_B);
+      p->d_stage_B = nullptr;
+      p->stage_B = 0;
+      VCSR_CUDA(cudaMalloc(&p->d_stage_B, nb));
+      p->stage_B = nb;
     }
-    if (banded) {
-      if (!p->down) VCSR_CUDA(cudaStreamCreateWithFlags(&p->down, cudaStreamNonBlocking));
-      if (!p->comp) VCSR_CUDA(cudaStreamCreateWithFlags(&p->comp, cudaStreamNonBlocking));
-      while ((int)p->chunk_done.size() < 2 * P) {
-        cudaEvent_t e;
-        VCSR_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
-        p->chunk_done.push_back(e);
+    if (nc > p->stage_C) {
+      cudaFree(p->d_stage_C);
+      p->d_stage_C = nullptr;
+      p->stage_C = 0;
+      VCSR_CUDA(cudaMalloc(&p->d_stage_C, nc));
+      p->stage_C = nc;
+    }
+    constexpr size_t kPipelineBytes = (size_t)8 << 20;
+    if (O > 0 && p->N > 0 && p->M > 0 && nb + nc >= kPipelineBytes && !p->rpanels.empty() &&
+        !(p->n_split_units > 0 && O > p->pstride)) {
+      // Row pipeline for banded matrices: B goes up in P contiguous row chunks
+      // on `stream`, chunk j ending at the highest column that row panels
+      // 0..j read (the last one at N); row panel j runs on the plan's compute
+      // stream as soon as chunk j is up, and its C rows go back on the
+      // download stream.  Used when no panel reads B rows beyond the next
+      // equal 1/P share of B, so that the chunks stay balanced and uploads,
+      // products and downloads overlap.
+      const int P = (int)p->rpanels.size();
+      const int per = (p->N + P - 1) / P;
+      bool banded = true;
+      std::vector<int> cend(P);
+      for (int j = 0, c = 0; j < P; ++j) {
+        const int cm = p->rpanels[j].col_max;
+        if (j + 1 < P && cm >= 0 && cm / per > j + 1) banded = false;
+        c = std::max(c, std::min(p->N, cm + 1));
+        cend[j] = j == P - 1 ? p->N : c;
       }
-      const size_t row_b = sizeof(float) * (size_t)O;
-      vcsr_status status = VCSR_OK;
-      cudaError_t e = cudaSuccess;
-      for (int i = 0; i < P && e == cudaSuccess; ++i) {
-        const int r0 = i == 0 ? 0 : cend[i - 1], r1 = cend[i];
-        if (r1 > r0)
-          e = cudaMemcpyAsync(p->d_stage_B + (size_t)r0 * O, hB + (size_t)r0 * O,
-                              row_b * (r1 - r0), cudaMemcpyHostToDevice, st);
-        if (e == cudaSuccess) e = cudaEventRecord(p->chunk_done[i], st);
-      }
-      if (e != cudaSuccess) status = fail(VCSR_ERR_CUDA, "row upload: %s", cudaGetErrorString(e));
-      for (int j = 0; j < P && status == VCSR_OK; ++j) {
-        const auto &rp = p->rpanels[j];
-        e = cudaStreamWaitEvent(p->comp, p->chunk_done[j], 0);
-        if (e != cudaSuccess) {
-          status = fail(VCSR_ERR_CUDA, "row panel wait: %s", cudaGetErrorString(e));
-          break;
+      if (banded) {
+        if (!p->down) VCSR_CUDA(cudaStreamCreateWithFlags(&p->down, cudaStreamNonBlocking));
+        if (!p->comp) VCSR_CUDA(cudaStreamCreateWithFlags(&p->comp, cudaStreamNonBlocking));
+        while ((int)p->chunk_done.size() < 2 * P) {
+          cudaEvent_t e;
+          VCSR_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+          p->chunk_done.push_back(e);
         }
-        vcsr::PanelDevView v = view(p);
-        v.batches += rp.b0;
-        v.n_batches = rp.b1 - rp.b0;
-        v.long_idx += rp.l0;
-        v.n_long = rp.l1 - rp.l0;
-        status = vcsr::launch_panel_spmm(v, false, p->d_stage_B, O, p->d_stage_C, O, O, p->comp,
-                                         nullptr, p->side, p->fork, p->join);
-        if (status != VCSR_OK) break;
-        e = cudaEventRecord(p->chunk_done[P + j], p->comp);
-        if (e == cudaSuccess) e = cudaStreamWaitEvent(p->down, p->chunk_done[P + j], 0);
-        if (e == cudaSuccess && rp.row1 > rp.row0)
-          e = cudaMemcpyAsync(hC + (size_t)rp.row0 * O, p->d_stage_C + (size_t)rp.row0 * O,
-                              row_b * (rp.row1 - rp.row0), cudaMemcpyDeviceToHost, p->down);
-        if (e != cudaSuccess) status = fail(VCSR_ERR_CUDA, "row download: %s", cudaGetErrorString(e));
+        const size_t row_b = sizeof(float) * (size_t)O;
+        vcsr_status status = VCSR_OK;
+        cudaError_t e = cudaSuccess;
+        for (int i = 0; i < P && e == cudaSuccess; ++i) {
+          const int r0 = i == 0 ? 0 : cend[i - 1], r1 = cend[i];
+          if (r1 > r0)
+            e = cudaMemcpyAsync(p->d_stage_B + (size_t)r0 * O, hB + (size_t)r0 * O,
+                                row_b * (r1 - r0), cudaMemcpyHostToDevice, st);
+          if (e == cudaSuccess) e = cudaEventRecord(p->chunk_done[i], st);
+        }
+        if (e != cudaSuccess) status = fail(VCSR_ERR_CUDA, "row upload: %s", cudaGetErrorString(e));
+        for (int j = 0; j < P && status == VCSR_OK; ++j) {
+          const auto &rp = p->rpanels[j];
+          e = cudaStreamWaitEvent(p->comp, p->chunk_done[j], 0);
+          if (e != cudaSuccess) {
+            status = fail(VCSR_ERR_CUDA, "row panel wait: %s", cudaGetErrorString(e));
+            break;
+          }
+          vcsr::PanelDevView v = view(p);
+          v.batches += rp.b0;
+          v.n_batches = rp.b1 - rp.b0;
+          v.long_idx += rp.l0;
+          v.n_long = rp.l1 - rp.l0;
+          status = vcsr::launch_panel_spmm(v, false, p->d_stage_B, O, p->d_stage_C, O, O, p->comp,
+                                           nullptr, p->side, p->fork, p->join);
+          if (status != VCSR_OK) break;
+          e = cudaEventRecord(p->chunk_done[P + j], p->comp);
+          if (e == cudaSuccess) e = cudaStreamWaitEvent(p->down, p->chunk_done[P + j], 0);
+          if (e == cudaSuccess && rp.row1 > rp.row0)
+            e = cudaMemcpyAsync(hC + (size_t)rp.row0 * O, p->d_stage_C + (size_t)rp.row0 * O,
+                                row_b * (rp.row1 - rp.row0), cudaMemcpyDeviceToHost, p->down);
+          if (e != cudaSuccess) status = fail(VCSR_ERR_CUDA, "row download: %s", cudaGetErrorString(e));
+        }
+        // every stream drains before returning, also after an error
+        const cudaError_t e1 = cudaStreamSynchronize(p->down), e2 = cudaStreamSynchronize(p->comp),
+                          e3 = cudaStreamSynchronize(st);
+        if (status != VCSR_OK) return status;
+        if (e1 != cudaSuccess || e2 != cudaSuccess || e3 != cudaSuccess)
+          return fail(VCSR_ERR_CUDA, "row pipeline: %s",
+                      cudaGetErrorString(e1 != cudaSuccess ? e1 : (e2 != cudaSuccess ? e2 : e3)));
+        return VCSR_OK;
       }
-      // every stream drains before returning, also after an error
-      const cudaError_t e1 = cudaStreamSynchronize(p->down), e2 = cudaStreamSynchronize(p->comp),
-                        e3 = cudaStreamSynchronize(st);
-      if (status != VCSR_OK) return status;
-      if (e1 != cudaSuccess || e2 != cudaSuccess || e3 != cudaSuccess)
-        return fail(VCSR_ERR_CUDA, "row pipeline: %s",
-                    cudaGetErrorString(e1 != cudaSuccess ? e1 : (e2 != cudaSuccess ? e2 : e3)));
-      return VCSR_OK;
     }
-  }
-  // Columns of B and C split into chunks are independent products
-  // (C[:, chunk] = A * B[:, chunk]).  With large buffers the call runs as a
-  // pipeline of up to four chunks: the chunks go up back to back on
-  // `stream`, chunk k is multiplied on the plan's compute stream once it is
-  // up and downloaded on the plan's download stream once multiplied, so the
-  // two PCIe directions overlap and no upload waits for a product.  Chunk
-  // copies are 2-D
-  // (w floats out of every row of O); measured on B200 hosts, rows of at
-  // least 256 bytes keep both directions at full speed (128-byte rows lose
-  // a third), so a chunk is at least 64 floats wide.
-  int W = O;
-  if (O >= 128 && nb + nc >= kPipelineBytes) {
-    const int nch = std::min(4, O / 64);
-    W = (int)(((O + nch - 1) / nch + 3) & ~3);
-  }
-  const int n_chunks = O > 0 ? (O + W - 1) / W : 0;
-  if (n_chunks <= 1) {
-    if (nb) VCSR_CUDA(cudaMemcpyAsync(p->d_stage_B, hB, nb, cudaMemcpyHostToDevice, st));
-    VCSR_TRY(vcsr_spmm(p, p->d_stage_B, O, p->d_stage_C, O, O, stream, nullptr));
-    if (nc) VCSR_CUDA(cudaMemcpyAsync(hC, p->d_stage_C, nc, cudaMemcpyDeviceToHost, st));
-    VCSR_CUDA(cudaStreamSynchronize(st));
+    // Columns of B and C split into chunks are independent products
+    // (C[:, chunk] = A * B[:, chunk]).  With large buffers the call runs as a
+    // pipeline of up to four chunks: the chunks go up back to back on
+    // `stream`, chunk k is multiplied on the plan's compute stream once it is
+    // up and downloaded on the plan's download stream once multiplied, so the
+    // two PCIe directions overlap and no upload waits for a product.  Chunk
+    // copies are 2-D
+    // (w floats out of every row of O); measured on B200 hosts, rows of at
+    // least 256 bytes keep both directions at full speed (128-byte rows lose
+    // a third), so a chunk is at least 64 floats wide.
+    int W = O;
+    if (O >= 128 && nb + nc >= kPipelineBytes) {
+      const int nch = std::min(4, O / 64);
+      W = (int)(((O + nch - 1) / nch + 3) & ~3);
+    }
+    const int n_chunks = O > 0 ? (O + W - 1) / W : 0;
+    if (n_chunks <= 1) {
+      if (nb) VCSR_CUDA(cudaMemcpyAsync(p->d_stage_B, hB, nb, cudaMemcpyHostToDevice, st));
+      VCSR_TRY(vcsr_spmm(p, p->d_stage_B, O, p->d_stage_C, O, O, stream, nullptr));
+      if (nc) VCSR_CUDA(cudaMemcpyAsync(hC, p->d_stage_C, nc, cudaMemcpyDeviceToHost, st));
+      VCSR_CUDA(cudaStreamSynchronize(st));
+      return p->d_err ? vcsr_plan_check(p, stream) : VCSR_OK;
+    }
+    if (!p->down) VCSR_CUDA(cudaStreamCreateWithFlags(&p->down, cudaStreamNonBlocking));
+    if (!p->comp) VCSR_CUDA(cudaStreamCreateWithFlags(&p->comp, cudaStreamNonBlocking));
+    while ((int)p->chunk_done.size() < 2 * n_chunks) {
+      cudaEvent_t e;
+      VCSR_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+      p->chunk_done.push_back(e);
+    }
+    const size_t pitch = sizeof(float) * (size_t)O;
+    vcsr_status status = VCSR_OK;
+    cudaError_t e = cudaSuccess;
+    for (int k = 0; k < n_chunks && e == cudaSuccess; ++k) {  // uploads, back to back
+      const int o0 = k * W, w = std::min(W, O - o0);
+      if (p->N > 0)
+        e = cudaMemcpy2DAsync(p->d_stage_B + o0, pitch, hB + o0, pitch, sizeof(float) * w,
+                              (size_t)p->N, cudaMemcpyHostToDevice, st);
+      if (e == cudaSuccess) e = cudaEventRecord(p->chunk_done[k], st);
+    }
+    if (e != cudaSuccess) status = fail(VCSR_ERR_CUDA, "chunk upload: %s", cudaGetErrorString(e));
+    for (int k = 0; k < n_chunks && status == VCSR_OK; ++k) {
+      const int o0 = k * W, w = std::min(W, O - o0);
+      e = cudaStreamWaitEvent(p->comp, p->chunk_done[k], 0);
+      if (e != cudaSuccess) {
+        status = fail(VCSR_ERR_CUDA, "chunk wait: %s", cudaGetErrorString(e));
+        break;
+      }
+      status = vcsr_spmm(p, p->d_stage_B + o0, O, p->d_stage_C + o0, O, w, p->comp, nullptr);
+      if (status != VCSR_OK) break;
+      e = cudaEventRecord(p->chunk_done[n_chunks + k], p->comp);
+      if (e == cudaSuccess) e = cudaStreamWaitEvent(p->down, p->chunk_done[n_chunks + k], 0);
+      if (e == cudaSuccess && p->M > 0)
+        e = cudaMemcpy2DAsync(hC + o0, pitch, p->d_stage_C + o0, pitch, sizeof(float) * w,
+                              (size_t)p->M, cudaMemcpyDeviceToHost, p->down);
+      if (e != cudaSuccess) status = fail(VCSR_ERR_CUDA, "chunk download: %s", cudaGetErrorString(e));
+    }
+    // every stream drains before returning, also after an error
+    const cudaError_t e0 = cudaStreamSynchronize(p->comp);
+    const cudaError_t e1 = cudaStreamSynchronize(p->down), e2 = cudaStreamSynchronize(st);
+    if (status != VCSR_OK) return status;
+    if (e0 != cudaSuccess || e1 != cudaSuccess || e2 != cudaSuccess)
+      return fail(VCSR_ERR_CUDA, "host entry point: %s",
+                  cudaGetErrorString(e0 != cudaSuccess ? e0 : (e1 != cudaSuccess ? e1 : e2)));
     return p->d_err ? vcsr_plan_check(p, stream) : VCSR_OK;
-  }
-  if (!p->down) VCSR_CUDA(cudaStreamCreateWithFlags(&p->down, cudaStreamNonBlocking));
-  if (!p->comp) VCSR_CUDA(cudaStreamCreateWithFlags(&p->comp, cudaStreamNonBlocking));
-  while ((int)p->chunk_done.size() < 2 * n_chunks) {
-    cudaEvent_t e;
-    VCSR_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
-    p->chunk_done.push_back(e);
-  }
-  const size_t pitch = sizeof(float) * (size_t)O;
-  vcsr_status status = VCSR_OK;
-  cudaError_t e = cudaSuccess;
-  for (int k = 0; k < n_chunks && e == cudaSuccess; ++k) {  // uploads, back to back
-    const int o0 = k * W, w = std::min(W, O - o0);
-    if (p->N > 0)
-      e = cudaMemcpy2DAsync(p->d_stage_B + o0, pitch, hB + o0, pitch, sizeof(float) * w,
-                            (size_t)p->N, cudaMemcpyHostToDevice, st);
-    if (e == cudaSuccess) e = cudaEventRecord(p->chunk_done[k], st);
-  }
-  if (e != cudaSuccess) status = fail(VCSR_ERR_CUDA, "chunk upload: %s", cudaGetErrorString(e));
-  for (int k = 0; k < n_chunks && status == VCSR_OK; ++k) {
-    const int o0 = k * W, w = std::min(W, O - o0);
-    e = cudaStreamWaitEvent(p->comp, p->chunk_done[k], 0);
-    if (e != cudaSuccess) {
-      status = fail(VCSR_ERR_CUDA, "chunk wait: %s", cudaGetErrorString(e));
-      break;
-    }
-    status = vcsr_spmm(p, p->d_stage_B + o0, O, p->d_stage_C + o0, O, w, p->comp, nullptr);
-    if (status != VCSR_OK) break;
-    e = cudaEventRecord(p->chunk_done[n_chunks + k], p->comp);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(p->down, p->chunk_done[n_chunks + k], 0);
-    if (e == cudaSuccess && p->M > 0)
-      e = cudaMemcpy2DAsync(hC + o0, pitch, p->d_stage_C + o0, pitch, sizeof(float) * w,
-                            (size_t)p->M, cudaMemcpyDeviceToHost, p->down);
-    if (e != cudaSuccess) status = fail(VCSR_ERR_CUDA, "chunk download: %s", cudaGetErrorString(e));
-  }
-  // every stream drains before returning, also after an error
-  const cudaError_t e0 = cudaStreamSynchronize(p->comp);
-  const cudaError_t e1 = cudaStreamSynchronize(p->down), e2 = cudaStreamSynchronize(st);
-  if (status != VCSR_OK) return status;
-  if (e0 != cudaSuccess || e1 != cudaSuccess || e2 != cudaSuccess)
-    return fail(VCSR_ERR_CUDA, "host entry point: %s",
-                cudaGetErrorString(e0 != cudaSuccess ? e0 : (e1 != cudaSuccess ? e1 : e2)));
-  return p->d_err ? vcsr_plan_check(p, stream) : VCSR_OK;
+  });
+}
+
+vcsr_status vcsr_plan_test_withhold_signal(vcsr_plan *p) {
+  vcsr::clear_error();
+  if (!p) return fail(VCSR_ERR_INVALID, "null plan");
+  if (p->n_panel_rb == 0)
+    return fail(VCSR_ERR_UNSUPPORTED, "the plan has no TF32 panels (no barrier waits)");
+  p->tc_inject.store(1);
+  return VCSR_OK;
 }
 
 vcsr_status vcsr_plan_check(vcsr_plan *p, vcsr_stream_t stream) {

@@ -3,6 +3,7 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 #include <vector>
 
@@ -20,6 +21,7 @@ struct vcsr_plan {
   int n_units = 0, n_split_units = 0, n_split_vectors = 0;
   int *d_ucol = nullptr;
   float *d_uval = nullptr;
+  unsigned *d_umask = nullptr;  // R > 1: which rows of a vector hold each union entry
   int4 *d_units = nullptr;
   int4 *d_batches = nullptr;
   int *d_long = nullptr, *d_vec_ptr = nullptr;
@@ -37,6 +39,9 @@ struct vcsr_plan {
   int *d_rb_row = nullptr, *d_rb_ptr = nullptr, *d_blk_col = nullptr, *d_err = nullptr;
   float *d_blk_val = nullptr;
   int n_panel_rb = 0, n_panel_blocks = 0;
+  // test hook (vcsr_plan_test_withhold_signal): the next TF32 panel launch
+  // withholds one barrier signal; one-shot
+  mutable std::atomic<int> tc_inject{0};
   int64_t panel_nnz = 0;
   // side stream and events for running long units beside short ones
   cudaStream_t side = nullptr;

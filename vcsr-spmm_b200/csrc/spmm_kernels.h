@@ -11,6 +11,10 @@ namespace vcsr {
 struct PanelDevView {
   const int *ucol = nullptr;
   const float *uval = nullptr;
+  // R > 1: per union column, bit r set when row r of the vector holds the
+  // entry (the others are padding zeros).  Read only when a padded sum came
+  // out NaN and the rows are recomputed over their own entries.
+  const unsigned *umask = nullptr;
   const int4 *units = nullptr;    // {vector, begin, end, split slot or -1}
   const int *row_ptr = nullptr;   // CSR mode only
   int n_units = 0;

@@ -325,11 +325,82 @@ __device__ __forceinline__ void load_group(const TB *__restrict__ Bk, int ldb,
 }
 
 // Vector boundaries inside a batch of consecutive vectors: `v` is the vector
-// being summed, `ve` the union index where it ends (svp holds vec_ptr[v0..v1]).
+// being summed, [vb, ve) its union range (svp holds vec_ptr[v0..v1]).
 struct BatchCursor {
   int v, ve, v0;
   const int *svp;
+  int vb;
 };
+
+// Non-finite padding.  A vector of R > 1 rows multiplies, for each union
+// column, all R rows' values by the B row, zeros included where a row lacks
+// the column.  For finite B that adds exact zeros, but a padding zero times an
+// Inf or NaN of B is NaN, in a row whose CSR sum (src/kernels.cu:27-31) never
+// reads that B row.  Such a wrong value is always NaN, so a lane whose sums
+// hold a NaN (or an Inf - Inf: the check is one sum) recomputes its columns of
+// the vector's rows over the rows' own entries (umask), in union order, which
+// is each row's CSR order.  The common, finite case costs one sum per store.
+template <int R, int NV, int VW>
+__device__ __forceinline__ bool sums_have_nan(const typename VecT<VW>::T (&o)[R][NV]) {
+  float s = 0.f;
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      if constexpr (VW == 4) {
+        s += (o[r][v].x + o[r][v].y) + (o[r][v].z + o[r][v].w);
+      } else {
+        s += o[r][v];
+      }
+    }
+  return s != s;
+}
+
+// This lane's columns kk[] of the vector's R rows over union columns
+// [begin, end), multiplying only the entries each row holds: the CSR sum.
+template <int R, int NV, int VW, class TB>
+__device__ __forceinline__ void exact_rows(const PanelDevView &P, const TB *__restrict__ B,
+                                           int ldb, int begin, int end, const int (&kk)[NV],
+                                           const bool (&ok)[NV],
+                                           typename VecT<VW>::T (&out)[R][NV]) {
+  using V = VecT<VW>;
+  typename V::T s[R][NV];
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+#pragma unroll
+    for (int v = 0; v < NV; ++v) s[r][v] = V::zero();
+  for (int j = begin; j < end; ++j) {
+    const int c = __ldg(P.ucol + j);
+    const unsigned m = __ldg(P.umask + j);
+    typename V::T b[NV];
+#pragma unroll
+    for (int v = 0; v < NV; ++v)
+      b[v] = ok[v] ? LdB<VW>::ld(B + (size_t)c * ldb + kk[v]) : V::zero();
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      if ((m >> r) & 1u) {
+        const float a = __ldg(P.uval + (size_t)j * R + r);
+#pragma unroll
+        for (int v = 0; v < NV; ++v) s[r][v] = V::fma(a, b[v], s[r][v]);
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+#pragma unroll
+    for (int v = 0; v < NV; ++v) out[r][v] = s[r][v];
+}
+
+// Replace a lane's padded sums by the exact ones when they hold a NaN.
+template <int R, int NV, int VW, class TB>
+__device__ __forceinline__ void settle_rows(const PanelDevView &P, const TB *__restrict__ B,
+                                            int ldb, int begin, int end, const int (&kk)[NV],
+                                            const bool (&ok)[NV],
+                                            typename VecT<VW>::T (&o)[R][NV]) {
+  if constexpr (R > 1) {
+    if (sums_have_nan<R, NV, VW>(o)) exact_rows<R, NV, VW, TB>(P, B, ldb, begin, end, kk, ok, o);
+  }
+}
 
 template <int R, int NV, int VW>
 __device__ __forceinline__ void store_rows(float *__restrict__ C, int ldc, int M, int row0,
@@ -348,31 +419,36 @@ __device__ __forceinline__ void store_rows(float *__restrict__ C, int ldc, int M
 }
 
 // Write the finished vector(s) before union index `a` and start the next.
-template <int R, int NV, int VW>
+template <int R, int NV, int VW, class TB>
 __device__ __forceinline__ void cross_boundaries(int a, BatchCursor &bc, Acc<R, NV, VW> &acc,
-                                                 float *__restrict__ C, int ldc, int M,
+                                                 const PanelDevView &P, const TB *__restrict__ B,
+                                                 int ldb, float *__restrict__ C, int ldc,
                                                  const int (&kk)[NV], const bool (&ok)[NV]) {
   while (a >= bc.ve) {
     typename VecT<VW>::T o[R][NV];
     acc.store(o);
-    store_rows<R, NV, VW>(C, ldc, M, bc.v * R, kk, ok, o);
+    settle_rows<R, NV, VW, TB>(P, B, ldb, bc.vb, bc.ve, kk, ok, o);
+    store_rows<R, NV, VW>(C, ldc, P.M, bc.v * R, kk, ok, o);
     acc.zero();
     ++bc.v;
+    bc.vb = bc.ve;
     bc.ve = bc.svp[bc.v - bc.v0 + 1];
   }
 }
 
-template <int R, int NV, int VW, int UN, bool FULL, bool BATCH>
+template <int R, int NV, int VW, int UN, bool FULL, bool BATCH, class TB>
 __device__ __forceinline__ void fma_group(const float *sval, int j0, int step, int n,
                                           const typename VecT<VW>::T (&b)[UN][NV],
                                           Acc<R, NV, VW> &acc, int cbase, BatchCursor &bc,
-                                          float *__restrict__ C, int ldc, int M,
+                                          const PanelDevView &P, const TB *__restrict__ B,
+                                          int ldb, float *__restrict__ C, int ldc,
                                           const int (&kk)[NV], const bool (&ok)[NV]) {
 #pragma unroll
   for (int q = 0; q < UN; ++q) {
     const int j = j0 + q * step;
     if (FULL || j < n) {
-      if constexpr (BATCH) cross_boundaries<R, NV, VW>(cbase + j, bc, acc, C, ldc, M, kk, ok);
+      if constexpr (BATCH)
+        cross_boundaries<R, NV, VW, TB>(cbase + j, bc, acc, P, B, ldb, C, ldc, kk, ok);
       float a[R];
       load_vals_smem<R>(sval, j, a);
       acc.fma(a, b[q]);
@@ -430,8 +506,8 @@ __device__ __forceinline__ void walk_unit(
       for (int g = 0; g < nfull; g += 2) {
         if (g + 1 < nfull)
           load_group<NV, VW, UN, true, TB>(Bk, ldb, scol, j + gstep, ncg, n, ok, vstride, b1);
-        fma_group<R, NV, VW, UN, true, BATCH>(sval, j, ncg, n, b0, acc, c0, bc, C, ldc,
-                                              P.M, kk, ok);
+        fma_group<R, NV, VW, UN, true, BATCH, TB>(sval, j, ncg, n, b0, acc, c0, bc, P, B, ldb,
+                                                  C, ldc, kk, ok);
         if (g + 1 >= nfull) {
           j += gstep;
           break;
@@ -439,23 +515,26 @@ __device__ __forceinline__ void walk_unit(
         if (g + 2 < nfull)
           load_group<NV, VW, UN, true, TB>(Bk, ldb, scol, j + 2 * gstep, ncg, n, ok, vstride,
                                        b0);
-        fma_group<R, NV, VW, UN, true, BATCH>(sval, j + gstep, ncg, n, b1, acc, c0, bc, C,
-                                              ldc, P.M, kk, ok);
+        fma_group<R, NV, VW, UN, true, BATCH, TB>(sval, j + gstep, ncg, n, b1, acc, c0, bc, P,
+                                                  B, ldb, C, ldc, kk, ok);
         j += 2 * gstep;
       }
       if (j < n) {
         load_group<NV, VW, UN, false, TB>(Bk, ldb, scol, j, ncg, n, ok, vstride, b0);
-        fma_group<R, NV, VW, UN, false, BATCH>(sval, j, ncg, n, b0, acc, c0, bc, C, ldc,
-                                               P.M, kk, ok);
+        fma_group<R, NV, VW, UN, false, BATCH, TB>(sval, j, ncg, n, b0, acc, c0, bc, P, B, ldb,
+                                                   C, ldc, kk, ok);
       }
       __syncwarp(tmask);  // everyone is done with `cur` before it is refilled
       cur ^= 1;
     }
   }
   if constexpr (BATCH) {
-    // the last vector and any empty vectors after it
+    // the last vector (union columns [bc.vb, end)) and any empty vectors
+    // after it
     while (bc.v < v1) {
       acc.store(out);
+      settle_rows<R, NV, VW, TB>(P, B, ldb, bc.vb, end, kk, ok, out);
+      bc.vb = end;
       store_rows<R, NV, VW>(C, ldc, P.M, bc.v * R, kk, ok, out);
       acc.zero();
       ++bc.v;
@@ -606,16 +685,16 @@ __global__ void __launch_bounds__(256, (min_blocks_for<R, NV, VW>()))
       ok[v] = kk[v] < O;
     }
     Tv acc[R][NV];
-    BatchCursor bc{0, 0, 0, nullptr};
+    BatchCursor bc{0, 0, 0, nullptr, 0};
     if constexpr (kBatch) {
       const int4 bt = __ldg(P.batches + s);  // {v0, v1, first column, end column}
       if (bt.y - bt.x == 1) {
         // one vector: it ends where the batch ends, no boundaries to stage
-        bc = BatchCursor{bt.x, bt.w, bt.x, svp};
+        bc = BatchCursor{bt.x, bt.w, bt.x, svp, bt.z};
       } else {
         for (int i = sl; i <= bt.y - bt.x; i += L) svp[i] = __ldg(P.vec_ptr + bt.x + i);
         __syncwarp(submask);
-        bc = BatchCursor{bt.x, svp[1], bt.x, svp};
+        bc = BatchCursor{bt.x, svp[1], bt.x, svp, bt.z};
       }
       walk_unit<R, NV, VW, true>(P, B, ldb, bt.z, bt.w, kk, ok, 0, 1, sl, L, submask, L,
                                  chunk, bcol, bval, acc, bc, bt.y, C, ldc);
@@ -630,6 +709,7 @@ __global__ void __launch_bounds__(256, (min_blocks_for<R, NV, VW>()))
       }
       walk_unit<R, NV, VW, false>(P, B, ldb, U.y, U.z, kk, ok, 0, 1, sl, L, submask, L,
                                   chunk, bcol, bval, acc, bc, 0, C, ldc);
+      settle_rows<R, NV, VW, TB>(P, B, ldb, U.y, U.z, kk, ok, acc);
       store_rows<R, NV, VW>(C, ldc, P.M, U.x * R, kk, ok, acc);
     }
   }
@@ -667,10 +747,12 @@ __global__ void __launch_bounds__(256, (long_min_blocks_for<R, NV, VW>()))
       ok[v] = kk[v] < O;
     }
     Tv acc[R][NV];
-    BatchCursor bc{0, 0, 0, nullptr};
+    BatchCursor bc{0, 0, 0, nullptr, 0};
     const int4 U = __ldg(P.units + __ldg(P.long_idx + w));
     walk_unit<R, NV, VW, false>(P, B, ldb, U.y, U.z, kk, ok, sub, G, lane, 32, 0xffffffffu,
                                 L, wcols, wcol, wval, acc, bc, 0, C, ldc);
+    // every column group holds the unit's sums; group 0 stores them
+    if (sub == 0) settle_rows<R, NV, VW, TB>(P, B, ldb, U.y, U.z, kk, ok, acc);
     finish_unit<R, NV, VW>(P, C, ldc, U, ot, kk, ok, sub, G, 0, 0xffffffffu, acc);
   }
 }
@@ -788,9 +870,9 @@ namespace {
 // Resident CTAs per SM of (kernel, dynamic shared memory, device), asked of
 // the runtime once: the query (and the shared-memory attribute) cost host time
 // that a small launch would otherwise wait for on the GPU.
-vcsr_status resident_per_sm(KernelFn fn, int threads, size_t smem, int *per_sm) {
+vcsr_status resident_per_sm(const void *fn, int threads, size_t smem, int *per_sm) {
   struct Key {
-    KernelFn fn;
+    const void *fn;
     size_t smem;
     int dev;
   };
@@ -827,7 +909,7 @@ vcsr_status launch_one(KernelFn fn, const PanelDevView &P, long long team_items,
                        float *C, int ldc, int O, cudaStream_t st) {
   const int threads = 256;
   int per_sm = 0;
-  VCSR_TRY(resident_per_sm(fn, threads, smem, &per_sm));
+  VCSR_TRY(resident_per_sm(reinterpret_cast<const void *>(fn), threads, smem, &per_sm));
   const long long items = team_items * s.n_otiles;
   long long blocks = (items + (threads / 32) - 1) / (threads / 32);
   const long long cap = (long long)sm_count() * per_sm;
@@ -943,8 +1025,11 @@ namespace vcsr {
 namespace {
 
 // Rows longer than kSplit entries get a slot, a range of part slots and
-// their {slot, part} records; overflow sets an error bit and skips the row.
-__global__ void noalloc_classify_kernel(const int *__restrict__ rp, int M,
+// their {slot, part} records, and the slot's n_otiles tickets are zeroed;
+// overflow sets an error bit and skips the row.  Every part record below
+// min(parts reserved, kMaxParts) is written by this pass (-1 where a row did
+// not fit), so nothing of an earlier call is read.
+__global__ void noalloc_classify_kernel(const int *__restrict__ rp, int M, int n_otiles,
                                         unsigned char *S) {
   using namespace noalloc;
   int *ctrl = reinterpret_cast<int *>(S + kCtrl);
@@ -964,11 +1049,14 @@ __global__ void noalloc_classify_kernel(const int *__restrict__ rp, int M,
     if (base + np > kMaxParts) {
       atomicOr(&ctrl[1], 2);
       lr[s] = -1;
+      for (int p = base; p < kMaxParts; ++p) parts[p] = make_int2(-1, -1);
       continue;
     }
     lr[s] = r;
     sv[s] = make_int2(base, np);
     for (int p = 0; p < np; ++p) parts[base + p] = make_int2(s, p);
+    int *tk = reinterpret_cast<int *>(S + kTickets) + (size_t)s * n_otiles;
+    for (int t = 0; t < n_otiles; ++t) tk[t] = 0;
   }
 }
 
@@ -1048,7 +1136,7 @@ __global__ void __launch_bounds__(256, (min_blocks_for<1, NV, VW>()))
       ok[v] = kk[v] < O;
     }
     Tv acc[1][NV];
-    BatchCursor bc{0, 0, 0, nullptr};
+    BatchCursor bc{0, 0, 0, nullptr, 0};
     walk_unit<1, NV, VW, false>(P, B, ldb, U.y, U.z, kk, ok, cg, ncg, t, T, tmask, L, chk,
                                 bcol, bval, acc, bc, 0, C, ldc);
     finish_unit<1, NV, VW>(P, C, ldc, U, ot, kk, ok, cg, ncg, lead, tmask, acc);
@@ -1093,15 +1181,14 @@ extern "C" vcsr_status vcsr_csr_spmm_noalloc(int M, const int *d_row_ptr,
   unsigned char *S = nullptr;
   VCSR_TRY(noalloc_scratch(&S));
   cudaStream_t st = (cudaStream_t)stream;
-  // the counters, the part records and every ticket must start at zero / -1
-  VCSR_CUDA(cudaMemsetAsync(S + kCtrl, 0, 256, st));
-  VCSR_CUDA(cudaMemsetAsync(S + kParts, 0xff, 8 * (size_t)kMaxParts, st));
-  VCSR_CUDA(cudaMemsetAsync(S + kTickets, 0, 4 * (size_t)kMaxLong * kMaxO, st));
-  const int sms = sm_count();
-  noalloc_classify_kernel<<<sms * 4, 256, 0, st>>>(d_row_ptr, M, S);
-  VCSR_CUDA(cudaGetLastError());
   const bool vec4 = (O % 4 == 0) && ((uintptr_t)dB % 16 == 0) && ((uintptr_t)dC % 16 == 0);
   const LaunchShape s = pick_shape(O, 1, vec4);
+  // the three counters start at zero; the classify pass writes every part
+  // record and zeroes every ticket the product will use
+  VCSR_CUDA(cudaMemsetAsync(S + kCtrl, 0, 256, st));
+  const int sms = sm_count();
+  noalloc_classify_kernel<<<sms * 4, 256, 0, st>>>(d_row_ptr, M, s.n_otiles, S);
+  VCSR_CUDA(cudaGetLastError());
   using Fn = void (*)(const int *, const int *, const float *, int, const float *, int,
                       float *, int, int, int, int, int, int, unsigned char *);
   Fn fn = s.VW == 4 ? (s.NV == 1 ? (Fn)noalloc_spmm_kernel<1, 4> : (Fn)noalloc_spmm_kernel<2, 4>)
@@ -1109,10 +1196,8 @@ extern "C" vcsr_status vcsr_csr_spmm_noalloc(int M, const int *d_row_ptr,
   const int threads = 256, G = 32 >> s.lshift;
   const int chunk = stage_chunk_cols(1, G);
   const size_t smem = (size_t)(threads / 32) * 2 * G * chunk * 2 * 4;
-  if (smem > 48 * 1024)
-    VCSR_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  int per_sm = 0;
-  VCSR_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem));
+  int per_sm = 0;  // asked of the runtime once per (kernel, shared memory, device)
+  VCSR_TRY(resident_per_sm(reinterpret_cast<const void *>(fn), threads, smem, &per_sm));
   const long long items = ((long long)kMaxParts + (M + G - 1) / G) * s.n_otiles;
   long long blocks = (items + (threads / 32) - 1) / (threads / 32);
   const long long cap = (long long)sms * (per_sm > 0 ? per_sm : 1);

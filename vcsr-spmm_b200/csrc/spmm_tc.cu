@@ -67,6 +67,8 @@ constexpr int kThreads = 192;
 constexpr int kProducerWarp = 4, kMmaWarp = 5;
 constexpr uint32_t kTmemCols = 32;  // two 16-column accumulators
 constexpr long long kPollLimit = 1ll << 22;
+// The short limit of the one wait a test makes run out (TcView::inject).
+constexpr long long kTestPollLimit = 1ll << 12;
 
 // Where a bounded wait gave up (recorded in the plan's error word).
 enum WaitSite : int {
@@ -96,9 +98,10 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
 // limit ran out (the site is recorded) or another thread already reported a
 // failure.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
-                                          volatile int *abort_flag, int site) {
+                                          volatile int *abort_flag, int site,
+                                          long long limit = kPollLimit) {
   const uint32_t a = smem_u32(bar);
-  for (long long i = 0; i < kPollLimit; ++i) {
+  for (long long i = 0; i < limit; ++i) {
     uint32_t done;
     asm volatile(
         "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; "
@@ -304,7 +307,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (u == kG - 1) mma_commit(empty + s);
         }
         if (!ok) break;
-        mma_commit(dfull + buf);  // the plan lists only row blocks with dense blocks
+        // the plan lists only row blocks with dense blocks; a test may
+        // withhold block 0's first accumulator-ready signal (TcView::inject)
+        if (!(V.inject && blockIdx.x == 0 && lt == 0)) mma_commit(dfull + buf);
       }
       *consumed = (g + kG - 1) / kG;  // stages whose copies were waited for
       // every MMA issued by this thread has finished before TMEM is freed
@@ -318,7 +323,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = blockIdx.x; t < n_items; t += gridDim.x, ++lt) {
       const int oc = t / V.n_rb, rbi = t - oc * V.n_rb;
       const int buf = lt & 1;
-      if (!mbar_wait(dfull + buf, (uint32_t)((lt >> 1) & 1), abort_flag, kWaitAccFull)) break;
+      const long long lim = (V.inject && blockIdx.x == 0 && lt == 0) ? kTestPollLimit : kPollLimit;
+      if (!mbar_wait(dfull + buf, (uint32_t)((lt >> 1) & 1), abort_flag, kWaitAccFull, lim))
+        break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       uint32_t r[16];
       const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(buf * 16);

@@ -28,6 +28,9 @@ struct TcView {
   // first failure: wait site (1 stage full, 2 stage empty, 3 accumulator
   // full, 4 accumulator free) | block index << 4; 0 when none
   int *err = nullptr;
+  // test hook: block 0 withholds its first accumulator-ready signal, and the
+  // epilogue's wait for it gives up after a short bounded poll
+  int inject = 0;
 };
 
 size_t tc_smem_bytes();

@@ -256,172 +256,174 @@ int bits_for(uint32_t v) {
 
 extern "C" vcsr_status vcsr_build_vcsr(const vcsr_csr *d, int segw, int bundle,
                                        vcsr_vcsr *out, vcsr_stream_t stream) {
-  using namespace vcsr;
-  clear_error();
-  if (!d || !out) return fail(VCSR_ERR_INVALID, "null argument");
-  std::memset(out, 0, sizeof *out);
-  if (bundle <= 0) return fail(VCSR_ERR_INVALID, "bundle must be >0");
-  if (segw <= 0) return fail(VCSR_ERR_INVALID, "segw must be >0");
-  if (d->M < 0 || d->N < 0 || d->nnz < 0) return fail(VCSR_ERR_INVALID, "negative size");
-  cudaStream_t st = (cudaStream_t)stream;
-  const int M = d->M, N = d->N, nnz = d->nnz;
-  const int S = (int)ceil_div(N, segw);
-  Scratch sc(st);
-  out->M = M; out->N = N; out->segw = segw; out->bundle = bundle;
-  out->num_segments = S;
-  auto alloc_out = [&](int64_t G, int64_t P) -> vcsr_status {
-    VCSR_CUDA(cudaMalloc(&out->group_ptr, sizeof(int) * (size_t)(G + 1)));
-    VCSR_CUDA(cudaMalloc(&out->group_depth, sizeof(int) * (size_t)(G > 0 ? G : 1)));
-    VCSR_CUDA(cudaMalloc(&out->group_seg_base, sizeof(int) * (size_t)(G > 0 ? G : 1)));
-    VCSR_CUDA(cudaMalloc(&out->group_rows,
-                         sizeof(int) * (size_t)(G * bundle > 0 ? G * bundle : 1)));
-    VCSR_CUDA(cudaMalloc(&out->lcol, sizeof(int) * (size_t)(P > 0 ? P : 1)));
-    VCSR_CUDA(cudaMalloc(&out->val, sizeof(float) * (size_t)(P > 0 ? P : 1)));
-    VCSR_CUDA(cudaMalloc(&out->segment_group_start, sizeof(int) * ((size_t)S + 1)));
-    return VCSR_OK;
-  };
-  if (nnz == 0 || M == 0) {
-    vcsr_status s = alloc_out(0, 0);
-    if (s == VCSR_OK) {
-      cudaError_t e = cudaMemsetAsync(out->group_ptr, 0, sizeof(int), st);
-      if (e == cudaSuccess)
-        e = cudaMemsetAsync(out->segment_group_start, 0, sizeof(int) * ((size_t)S + 1), st);
-      if (e == cudaSuccess) e = cudaStreamSynchronize(st);
-      if (e != cudaSuccess) s = fail(VCSR_ERR_CUDA, "%s", cudaGetErrorString(e));
+  return vcsr::no_throw([&]() -> vcsr_status {
+    using namespace vcsr;
+    clear_error();
+    if (!d || !out) return fail(VCSR_ERR_INVALID, "null argument");
+    std::memset(out, 0, sizeof *out);
+    if (bundle <= 0) return fail(VCSR_ERR_INVALID, "bundle must be >0");
+    if (segw <= 0) return fail(VCSR_ERR_INVALID, "segw must be >0");
+    if (d->M < 0 || d->N < 0 || d->nnz < 0) return fail(VCSR_ERR_INVALID, "negative size");
+    cudaStream_t st = (cudaStream_t)stream;
+    const int M = d->M, N = d->N, nnz = d->nnz;
+    const int S = (int)ceil_div(N, segw);
+    Scratch sc(st);
+    out->M = M; out->N = N; out->segw = segw; out->bundle = bundle;
+    out->num_segments = S;
+    auto alloc_out = [&](int64_t G, int64_t P) -> vcsr_status {
+      VCSR_CUDA(cudaMalloc(&out->group_ptr, sizeof(int) * (size_t)(G + 1)));
+      VCSR_CUDA(cudaMalloc(&out->group_depth, sizeof(int) * (size_t)(G > 0 ? G : 1)));
+      VCSR_CUDA(cudaMalloc(&out->group_seg_base, sizeof(int) * (size_t)(G > 0 ? G : 1)));
+      VCSR_CUDA(cudaMalloc(&out->group_rows,
+                           sizeof(int) * (size_t)(G * bundle > 0 ? G * bundle : 1)));
+      VCSR_CUDA(cudaMalloc(&out->lcol, sizeof(int) * (size_t)(P > 0 ? P : 1)));
+      VCSR_CUDA(cudaMalloc(&out->val, sizeof(float) * (size_t)(P > 0 ? P : 1)));
+      VCSR_CUDA(cudaMalloc(&out->segment_group_start, sizeof(int) * ((size_t)S + 1)));
+      return VCSR_OK;
+    };
+    if (nnz == 0 || M == 0) {
+      vcsr_status s = alloc_out(0, 0);
+      if (s == VCSR_OK) {
+        cudaError_t e = cudaMemsetAsync(out->group_ptr, 0, sizeof(int), st);
+        if (e == cudaSuccess)
+          e = cudaMemsetAsync(out->segment_group_start, 0, sizeof(int) * ((size_t)S + 1), st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+        if (e != cudaSuccess) s = fail(VCSR_ERR_CUDA, "%s", cudaGetErrorString(e));
+      }
+      if (s != VCSR_OK) vcsr_vcsr_free(out, VCSR_DEVICE);
+      return s;
     }
-    if (s != VCSR_OK) vcsr_vcsr_free(out, VCSR_DEVICE);
-    return s;
-  }
-  vcsr_status s;
-  auto body = [&]() -> vcsr_status {
-    int *bad;
-    VCSR_TRY(sc.get(&bad, 1));
-    VCSR_CUDA(cudaMemsetAsync(bad, 0, sizeof(int), st));
-    validate_kernel<<<grid_for((int64_t)nnz + M + 1), 256, 0, st>>>(d->row_ptr, d->col,
-                                                                   M, N, nnz, bad);
-    VCSR_CUDA(cudaGetLastError());
-    int hbad = 0;
-    VCSR_CUDA(cudaMemcpyAsync(&hbad, bad, sizeof(int), cudaMemcpyDeviceToHost, st));
-    VCSR_CUDA(cudaStreamSynchronize(st));
-    if (hbad & 1) return fail(VCSR_ERR_INVALID, "row_ptr is not a valid CSR row pointer");
-    if (hbad & 2) return fail(VCSR_ERR_RANGE, "a column index lies outside [0, N)");
-    sorted_kernel<<<grid_for(M), 256, 0, st>>>(d->row_ptr, d->col, M, bad);
-    VCSR_CUDA(cudaGetLastError());
-    VCSR_CUDA(cudaMemcpyAsync(&hbad, bad, sizeof(int), cudaMemcpyDeviceToHost, st));
-    VCSR_CUDA(cudaStreamSynchronize(st));
-    if (hbad & 4)
-      return fail(VCSR_ERR_INVALID, "CSR rows must be sorted by column (coo_to_csr order)");
-    int *head, *idx, *dE;
-    VCSR_TRY(sc.get(&head, nnz));
-    VCSR_TRY(sc.get(&idx, nnz));
-    VCSR_TRY(sc.get(&dE, 2));
-    head_kernel<<<grid_for(nnz), 256, 0, st>>>(d->row_ptr, d->col, M, nnz, segw, head);
-    VCSR_CUDA(cudaGetLastError());
-    VCSR_TRY(scan_exclusive<int>(head, idx, nnz, dE, sc));
-    int E = 0;
-    VCSR_CUDA(cudaMemcpyAsync(&E, dE, sizeof(int), cudaMemcpyDeviceToHost, st));
-    VCSR_CUDA(cudaStreamSynchronize(st));
-    int *pr_row, *pr_seg, *pr_start, *pr_cnt, *maxc;
-    VCSR_TRY(sc.get(&pr_row, E));
-    VCSR_TRY(sc.get(&pr_seg, E));
-    VCSR_TRY(sc.get(&pr_start, E));
-    VCSR_TRY(sc.get(&pr_cnt, E));
-    VCSR_TRY(sc.get(&maxc, 1));
-    pairs_kernel<<<grid_for(nnz), 256, 0, st>>>(d->row_ptr, d->col, M, nnz, segw,
-                                                head, idx, pr_row, pr_seg, pr_start);
-    VCSR_CUDA(cudaGetLastError());
-    VCSR_CUDA(cudaMemsetAsync(maxc, 0, sizeof(int), st));
-    count_kernel<<<grid_for(E), 256, 0, st>>>(pr_start, E, nnz, pr_cnt, maxc);
-    VCSR_CUDA(cudaGetLastError());
-    int hmaxc = 0;
-    VCSR_CUDA(cudaMemcpyAsync(&hmaxc, maxc, sizeof(int), cudaMemcpyDeviceToHost, st));
-    VCSR_CUDA(cudaStreamSynchronize(st));
-    const int sbits = bits_for((uint32_t)(S > 0 ? S - 1 : 0));
-    const int cbits = bits_for((uint32_t)hmaxc);
-    if (sbits + cbits > 32)
-      return fail(VCSR_ERR_UNSUPPORTED, "segment/count keys exceed 32 bits");
-    uint32_t *k_seg, *k_pack, *k_tmp;
-    int *iota, *seg_count, *by_seg, *pack_order;
-    VCSR_TRY(sc.get(&k_seg, E));
-    VCSR_TRY(sc.get(&k_pack, E));
-    VCSR_TRY(sc.get(&k_tmp, E));
-    VCSR_TRY(sc.get(&iota, E));
-    VCSR_TRY(sc.get(&seg_count, S));
-    VCSR_TRY(sc.get(&by_seg, E));
-    VCSR_TRY(sc.get(&pack_order, E));
-    VCSR_CUDA(cudaMemsetAsync(seg_count, 0, sizeof(int) * (size_t)S, st));
-    keys_kernel<<<grid_for(E), 256, 0, st>>>(pr_seg, pr_cnt, E, cbits, hmaxc, k_seg,
-                                             k_pack, iota, seg_count);
-    VCSR_CUDA(cudaGetLastError());
-    VCSR_TRY(radix_sort_pairs(k_seg, iota, k_tmp, by_seg, E, sbits, sc));
-    VCSR_TRY(radix_sort_pairs(k_pack, iota, k_tmp, pack_order, E, sbits + cbits, sc));
-    int *seg_first, *ng, *g_first, *dG;
-    VCSR_TRY(sc.get(&seg_first, S));
-    VCSR_TRY(sc.get(&ng, S));
-    VCSR_TRY(sc.get(&g_first, (int64_t)S + 1));
-    VCSR_TRY(sc.get(&dG, 1));
-    VCSR_TRY(scan_exclusive<int>(seg_count, seg_first, S, nullptr, sc));
-    ngroups_kernel<<<grid_for(S), 256, 0, st>>>(seg_count, S, bundle, ng);
-    VCSR_CUDA(cudaGetLastError());
-    VCSR_TRY(scan_exclusive<int>(ng, g_first, S, dG, sc));
-    int G = 0;
-    VCSR_CUDA(cudaMemcpyAsync(&G, dG, sizeof(int), cudaMemcpyDeviceToHost, st));
-    VCSR_CUDA(cudaStreamSynchronize(st));
-    if ((int64_t)G * bundle > INT32_MAX)
-      return fail(VCSR_ERR_UNSUPPORTED, "G*bundle exceeds 32-bit indexing");
-    int *g_seg, *g_depth_tmp;
-    long long *g_slots, *g_ptr64, *dP;
-    VCSR_TRY(sc.get(&g_seg, G));
-    VCSR_TRY(sc.get(&g_depth_tmp, G));
-    VCSR_TRY(sc.get(&g_slots, G));
-    VCSR_TRY(sc.get(&g_ptr64, (int64_t)G + 1));
-    VCSR_TRY(sc.get(&dP, 1));
-    // group metadata into the outputs once sizes are known: depth first
-    int *g_seg_base_tmp;
-    VCSR_TRY(sc.get(&g_seg_base_tmp, G));
-    group_meta_kernel<<<grid_for((int64_t)S * 32), 256, 0, st>>>(
-        seg_first, seg_count, g_first, ng, S, bundle, segw, pack_order, pr_cnt, g_seg,
-        g_depth_tmp, g_seg_base_tmp, g_slots);
-    VCSR_CUDA(cudaGetLastError());
-    VCSR_TRY(scan_exclusive<long long>(g_slots, g_ptr64, G, dP, sc));
-    long long P = 0;
-    VCSR_CUDA(cudaMemcpyAsync(&P, dP, sizeof(long long), cudaMemcpyDeviceToHost, st));
-    VCSR_CUDA(cudaStreamSynchronize(st));
-    if (P > INT32_MAX) return fail(VCSR_ERR_UNSUPPORTED, "VCSR exceeds 32-bit slot indexing");
-    VCSR_TRY(alloc_out(G, P));
-    out->num_groups = G;
-    out->num_slots = P;
-    if (G > 0) {
-      narrow_kernel<<<grid_for(G), 256, 0, st>>>(g_ptr64, out->group_ptr, G);
+    vcsr_status s;
+    auto body = [&]() -> vcsr_status {
+      int *bad;
+      VCSR_TRY(sc.get(&bad, 1));
+      VCSR_CUDA(cudaMemsetAsync(bad, 0, sizeof(int), st));
+      validate_kernel<<<grid_for((int64_t)nnz + M + 1), 256, 0, st>>>(d->row_ptr, d->col,
+                                                                     M, N, nnz, bad);
       VCSR_CUDA(cudaGetLastError());
-      VCSR_CUDA(cudaMemcpyAsync(out->group_depth, g_depth_tmp, sizeof(int) * (size_t)G,
-                                cudaMemcpyDeviceToDevice, st));
-      VCSR_CUDA(cudaMemcpyAsync(out->group_seg_base, g_seg_base_tmp,
-                                sizeof(int) * (size_t)G, cudaMemcpyDeviceToDevice, st));
+      int hbad = 0;
+      VCSR_CUDA(cudaMemcpyAsync(&hbad, bad, sizeof(int), cudaMemcpyDeviceToHost, st));
+      VCSR_CUDA(cudaStreamSynchronize(st));
+      if (hbad & 1) return fail(VCSR_ERR_INVALID, "row_ptr is not a valid CSR row pointer");
+      if (hbad & 2) return fail(VCSR_ERR_RANGE, "a column index lies outside [0, N)");
+      sorted_kernel<<<grid_for(M), 256, 0, st>>>(d->row_ptr, d->col, M, bad);
+      VCSR_CUDA(cudaGetLastError());
+      VCSR_CUDA(cudaMemcpyAsync(&hbad, bad, sizeof(int), cudaMemcpyDeviceToHost, st));
+      VCSR_CUDA(cudaStreamSynchronize(st));
+      if (hbad & 4)
+        return fail(VCSR_ERR_INVALID, "CSR rows must be sorted by column (coo_to_csr order)");
+      int *head, *idx, *dE;
+      VCSR_TRY(sc.get(&head, nnz));
+      VCSR_TRY(sc.get(&idx, nnz));
+      VCSR_TRY(sc.get(&dE, 2));
+      head_kernel<<<grid_for(nnz), 256, 0, st>>>(d->row_ptr, d->col, M, nnz, segw, head);
+      VCSR_CUDA(cudaGetLastError());
+      VCSR_TRY(scan_exclusive<int>(head, idx, nnz, dE, sc));
+      int E = 0;
+      VCSR_CUDA(cudaMemcpyAsync(&E, dE, sizeof(int), cudaMemcpyDeviceToHost, st));
+      VCSR_CUDA(cudaStreamSynchronize(st));
+      int *pr_row, *pr_seg, *pr_start, *pr_cnt, *maxc;
+      VCSR_TRY(sc.get(&pr_row, E));
+      VCSR_TRY(sc.get(&pr_seg, E));
+      VCSR_TRY(sc.get(&pr_start, E));
+      VCSR_TRY(sc.get(&pr_cnt, E));
+      VCSR_TRY(sc.get(&maxc, 1));
+      pairs_kernel<<<grid_for(nnz), 256, 0, st>>>(d->row_ptr, d->col, M, nnz, segw,
+                                                  head, idx, pr_row, pr_seg, pr_start);
+      VCSR_CUDA(cudaGetLastError());
+      VCSR_CUDA(cudaMemsetAsync(maxc, 0, sizeof(int), st));
+      count_kernel<<<grid_for(E), 256, 0, st>>>(pr_start, E, nnz, pr_cnt, maxc);
+      VCSR_CUDA(cudaGetLastError());
+      int hmaxc = 0;
+      VCSR_CUDA(cudaMemcpyAsync(&hmaxc, maxc, sizeof(int), cudaMemcpyDeviceToHost, st));
+      VCSR_CUDA(cudaStreamSynchronize(st));
+      const int sbits = bits_for((uint32_t)(S > 0 ? S - 1 : 0));
+      const int cbits = bits_for((uint32_t)hmaxc);
+      if (sbits + cbits > 32)
+        return fail(VCSR_ERR_UNSUPPORTED, "segment/count keys exceed 32 bits");
+      uint32_t *k_seg, *k_pack, *k_tmp;
+      int *iota, *seg_count, *by_seg, *pack_order;
+      VCSR_TRY(sc.get(&k_seg, E));
+      VCSR_TRY(sc.get(&k_pack, E));
+      VCSR_TRY(sc.get(&k_tmp, E));
+      VCSR_TRY(sc.get(&iota, E));
+      VCSR_TRY(sc.get(&seg_count, S));
+      VCSR_TRY(sc.get(&by_seg, E));
+      VCSR_TRY(sc.get(&pack_order, E));
+      VCSR_CUDA(cudaMemsetAsync(seg_count, 0, sizeof(int) * (size_t)S, st));
+      keys_kernel<<<grid_for(E), 256, 0, st>>>(pr_seg, pr_cnt, E, cbits, hmaxc, k_seg,
+                                               k_pack, iota, seg_count);
+      VCSR_CUDA(cudaGetLastError());
+      VCSR_TRY(radix_sort_pairs(k_seg, iota, k_tmp, by_seg, E, sbits, sc));
+      VCSR_TRY(radix_sort_pairs(k_pack, iota, k_tmp, pack_order, E, sbits + cbits, sc));
+      int *seg_first, *ng, *g_first, *dG;
+      VCSR_TRY(sc.get(&seg_first, S));
+      VCSR_TRY(sc.get(&ng, S));
+      VCSR_TRY(sc.get(&g_first, (int64_t)S + 1));
+      VCSR_TRY(sc.get(&dG, 1));
+      VCSR_TRY(scan_exclusive<int>(seg_count, seg_first, S, nullptr, sc));
+      ngroups_kernel<<<grid_for(S), 256, 0, st>>>(seg_count, S, bundle, ng);
+      VCSR_CUDA(cudaGetLastError());
+      VCSR_TRY(scan_exclusive<int>(ng, g_first, S, dG, sc));
+      int G = 0;
+      VCSR_CUDA(cudaMemcpyAsync(&G, dG, sizeof(int), cudaMemcpyDeviceToHost, st));
+      VCSR_CUDA(cudaStreamSynchronize(st));
+      if ((int64_t)G * bundle > INT32_MAX)
+        return fail(VCSR_ERR_UNSUPPORTED, "G*bundle exceeds 32-bit indexing");
+      int *g_seg, *g_depth_tmp;
+      long long *g_slots, *g_ptr64, *dP;
+      VCSR_TRY(sc.get(&g_seg, G));
+      VCSR_TRY(sc.get(&g_depth_tmp, G));
+      VCSR_TRY(sc.get(&g_slots, G));
+      VCSR_TRY(sc.get(&g_ptr64, (int64_t)G + 1));
+      VCSR_TRY(sc.get(&dP, 1));
+      // group metadata into the outputs once sizes are known: depth first
+      int *g_seg_base_tmp;
+      VCSR_TRY(sc.get(&g_seg_base_tmp, G));
+      group_meta_kernel<<<grid_for((int64_t)S * 32), 256, 0, st>>>(
+          seg_first, seg_count, g_first, ng, S, bundle, segw, pack_order, pr_cnt, g_seg,
+          g_depth_tmp, g_seg_base_tmp, g_slots);
+      VCSR_CUDA(cudaGetLastError());
+      VCSR_TRY(scan_exclusive<long long>(g_slots, g_ptr64, G, dP, sc));
+      long long P = 0;
+      VCSR_CUDA(cudaMemcpyAsync(&P, dP, sizeof(long long), cudaMemcpyDeviceToHost, st));
+      VCSR_CUDA(cudaStreamSynchronize(st));
+      if (P > INT32_MAX) return fail(VCSR_ERR_UNSUPPORTED, "VCSR exceeds 32-bit slot indexing");
+      VCSR_TRY(alloc_out(G, P));
+      out->num_groups = G;
+      out->num_slots = P;
+      if (G > 0) {
+        narrow_kernel<<<grid_for(G), 256, 0, st>>>(g_ptr64, out->group_ptr, G);
+        VCSR_CUDA(cudaGetLastError());
+        VCSR_CUDA(cudaMemcpyAsync(out->group_depth, g_depth_tmp, sizeof(int) * (size_t)G,
+                                  cudaMemcpyDeviceToDevice, st));
+        VCSR_CUDA(cudaMemcpyAsync(out->group_seg_base, g_seg_base_tmp,
+                                  sizeof(int) * (size_t)G, cudaMemcpyDeviceToDevice, st));
+      }
+      const int Pi = (int)P;
+      VCSR_CUDA(cudaMemcpyAsync(out->group_ptr + G, &Pi, sizeof(int),
+                                cudaMemcpyHostToDevice, st));
+      VCSR_CUDA(cudaMemcpyAsync(out->segment_group_start, g_first,
+                                sizeof(int) * (size_t)S, cudaMemcpyDeviceToDevice, st));
+      VCSR_CUDA(cudaMemcpyAsync(out->segment_group_start + S, &G, sizeof(int),
+                                cudaMemcpyHostToDevice, st));
+      pad_rows_kernel<<<grid_for((int64_t)S * 32), 256, 0, st>>>(
+          seg_first, seg_count, g_first, ng, S, M, bundle, by_seg, pr_row,
+          out->group_rows);
+      VCSR_CUDA(cudaGetLastError());
+      pack_kernel<<<grid_for((int64_t)G * 32), 256, 0, st>>>(
+          g_seg, out->group_depth, out->group_ptr, seg_first, seg_count, g_first, G, M,
+          bundle, segw, pack_order, pr_row, pr_cnt, pr_start, d->col, d->val,
+          out->group_rows, out->lcol, out->val);
+      VCSR_CUDA(cudaGetLastError());
+      VCSR_CUDA(cudaStreamSynchronize(st));  // host-side Pi/G copies end here
+      return VCSR_OK;
+    };
+    s = body();
+    if (s != VCSR_OK) {
+      cudaStreamSynchronize(st);
+      vcsr_vcsr_free(out, VCSR_DEVICE);
     }
-    const int Pi = (int)P;
-    VCSR_CUDA(cudaMemcpyAsync(out->group_ptr + G, &Pi, sizeof(int),
-                              cudaMemcpyHostToDevice, st));
-    VCSR_CUDA(cudaMemcpyAsync(out->segment_group_start, g_first,
-                              sizeof(int) * (size_t)S, cudaMemcpyDeviceToDevice, st));
-    VCSR_CUDA(cudaMemcpyAsync(out->segment_group_start + S, &G, sizeof(int),
-                              cudaMemcpyHostToDevice, st));
-    pad_rows_kernel<<<grid_for((int64_t)S * 32), 256, 0, st>>>(
-        seg_first, seg_count, g_first, ng, S, M, bundle, by_seg, pr_row,
-        out->group_rows);
-    VCSR_CUDA(cudaGetLastError());
-    pack_kernel<<<grid_for((int64_t)G * 32), 256, 0, st>>>(
-        g_seg, out->group_depth, out->group_ptr, seg_first, seg_count, g_first, G, M,
-        bundle, segw, pack_order, pr_row, pr_cnt, pr_start, d->col, d->val,
-        out->group_rows, out->lcol, out->val);
-    VCSR_CUDA(cudaGetLastError());
-    VCSR_CUDA(cudaStreamSynchronize(st));  // host-side Pi/G copies end here
-    return VCSR_OK;
-  };
-  s = body();
-  if (s != VCSR_OK) {
-    cudaStreamSynchronize(st);
-    vcsr_vcsr_free(out, VCSR_DEVICE);
-  }
-  return s;
+    return s;
+  });
 }

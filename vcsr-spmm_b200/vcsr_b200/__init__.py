@@ -115,6 +115,7 @@ _SIGS = {
     "vcsr_spmm_host": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
                                  C.c_void_p]),
     "vcsr_plan_check": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "vcsr_plan_test_withhold_signal": (C.c_int, [C.c_void_p]),
     "vcsr_plan_row_panels": (C.c_int, [C.c_void_p, C.POINTER(C.c_int), C.c_void_p,
                                        C.c_void_p, C.c_void_p]),
     "vcsr_spmm_row_panel": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p,
@@ -562,6 +563,11 @@ class Plan:
         """Synchronise and raise VcsrError (status 7) if a bounded wait of the
         plan's kernels ran out since the last check."""
         _check(lib().vcsr_plan_check(self._h, _stream(stream)))
+
+    def test_withhold_signal(self):
+        """Test hook: the next TF32 panel launch withholds one barrier signal,
+        so a bounded wait runs out and check() raises (status 7)."""
+        _check(lib().vcsr_plan_test_withhold_signal(self._h))
 
     def spmm_host(self, hB, hC, stream=None):
         """C = A*B with host buffers (H2D, SpMM, D2H, synchronise)."""

@@ -13,7 +13,37 @@ Two ways to own rows:
 """
 from __future__ import annotations
 
-from . import CSR, csr_row_panel, gen_csr, partition_rows
+from . import CSR, VcsrError, csr_row_panel, gen_csr, partition_rows
+
+STATUS_NCCL, STATUS_TIMEOUT = 6, 7
+
+
+def init_ranks(dist, backend: str = "nccl", timeout_s: float = 60.0, device=None):
+    """init_process_group with a bounded rendezvous and collective timeout.
+
+    A rank that never joins makes the others fail after about `timeout_s`
+    with VcsrError(status 7) instead of waiting for ever; the same timeout
+    bounds every later collective of the group."""
+    import datetime
+    kw = {"timeout": datetime.timedelta(seconds=timeout_s)}
+    if device is not None:
+        kw["device_id"] = device
+    try:
+        dist.init_process_group(backend, **kw)
+    except Exception as e:  # the store's rendezvous timed out or was refused
+        raise VcsrError(STATUS_TIMEOUT, f"rank rendezvous ({backend}) did not complete "
+                                        f"within {timeout_s:g} s: {e}") from e
+
+
+def _collective(what, fn):
+    """Run one collective; a peer that failed or left between steps turns
+    into VcsrError(status 6) on the ranks still running."""
+    try:
+        return fn()
+    except VcsrError:
+        raise
+    except Exception as e:
+        raise VcsrError(STATUS_NCCL, f"{what}: a peer rank failed, left or timed out: {e}") from e
 
 
 def rank_panel(config: str, size: int, seed: int, rank: int, world: int,
@@ -39,13 +69,13 @@ def global_nnz(panel: CSR, scaling: str, world: int, strong_total=None, dist=Non
         return panel.nnz * world if dist is None else panel.nnz
     import torch
     t = torch.tensor([panel.nnz], dtype=torch.int64, device=device)
-    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    _collective("global nnz", lambda: dist.all_reduce(t, op=dist.ReduceOp.SUM))
     return int(t.item())
 
 
 def broadcast_b(dist, tensor, src: int = 0):
     """Replicate B from `src` to every rank (one collective)."""
-    dist.broadcast(tensor, src=src)
+    _collective("broadcast of B", lambda: dist.broadcast(tensor, src=src))
     return tensor
 
 
@@ -55,14 +85,30 @@ def broadcast_and_multiply(dist, plan, dB, dC, src: int = 0, chunks: int = 4, st
     B goes out as `chunks` row chunks (asynchronous broadcasts, the same on
     every rank, so every rank takes the same collective steps); this rank
     multiplies each of its plan's row panels as soon as the chunk holding the
-    panel's highest column has arrived (waiting on a collective makes the
-    compute stream wait, not the host).  For banded matrices the products of
+    panel's highest column has arrived.  The broadcasts, the waits and the
+    products are all issued with `stream` (a torch.cuda.Stream or a raw
+    cudaStream_t; default the current stream) made the current stream: waiting
+    on a collective makes the CURRENT stream wait, so the products, enqueued
+    on that same stream, never read rows of B before they have arrived; the
+    host does not wait.  For banded matrices the products of
     the early panels run while later chunks are still on the wire.  A plan
     without row panels, or whose panels are not banded (some panel reads rows of
     B beyond the next chunk), waits for all of B and multiplies in one call.
     Returns the number of panels multiplied before the last chunk arrived.
     Measured on two B200s each chunk costs a collective's latency (~20 us), so
     this pays only when the product is long next to the broadcast."""
+    import contextlib
+    ctx = contextlib.nullcontext()
+    if stream is not None and getattr(dB, "is_cuda", False):
+        import torch
+        if isinstance(stream, int):
+            stream = torch.cuda.ExternalStream(stream)
+        ctx = torch.cuda.stream(stream)
+    with ctx:
+        return _broadcast_and_multiply(dist, plan, dB, dC, src, chunks, stream)
+
+
+def _broadcast_and_multiply(dist, plan, dB, dC, src, chunks, stream):
     N = dB.shape[0]
     per = -(-N // chunks) if N else 0
     works = []
@@ -98,5 +144,5 @@ def max_over_ranks(dist, value: float, device=None) -> float:
     """The slowest rank's time."""
     import torch
     t = torch.tensor([float(value)], dtype=torch.float64, device=device)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    _collective("max over ranks", lambda: dist.all_reduce(t, op=dist.ReduceOp.MAX))
     return float(t.item())
