@@ -6,20 +6,24 @@ flushed (256 MB write) before every timed step and each step is timed with
 CUDA events on the launching stream.  Under torchrun each rank owns one GPU;
 the reported time is the max over ranks.
 
-Workloads (synthetic stand-ins with the benchmark configurations' shapes):
-  fem (default)  62,451 x 62,451 FEM-style banded, ~4.0M nnz, O = 128.  With
-                 N GPUs every rank owns one such row panel (global A has
-                 N*62,451 rows), B is broadcast once from rank 0 over NCCL:
-                 weak scaling.
+Default workload: the north star's scaling configuration, R-MAT 2^22 at
+O = 256: A cut into N nnz-balanced row panels (one per rank),
+B replicated once by an NCCL broadcast (timed apart: `bcast_ms`), C panels
+disjoint, strong scaling.  At N = 1 the line also carries `fem_o128`, the
+FEM-banded O = 128 record (configs[1], the configuration the north star's
+roofline and cuSPARSE targets are stated on) with its own roofline, peers and
+end-to-end figure.
+
+Other workloads (`--workload`; synthetic stand-ins with the benchmark
+configurations' shapes):
+  fem            62,451 x 62,451 FEM-style banded, ~4.0M nnz, O = 128.  With
+                 N GPUs every rank owns one such panel: weak scaling.
   fem_o32 / fem_o512, uniform (O=32), powerlaw_o8 / powerlaw_o64,
   blockdense (O=512): single-panel variants (weak scaling under N GPUs).
   blockdense_tf32  the same matrix with its dense 16x16 blocks on the
                  tensor cores in TF32 (VCSR_PLAN_TF32_PANELS).
-  rmat_bf16, fem_bf16  B held in bfloat16, widened to FP32 on load
-                 (vcsr_spmm_bf16): half the B bytes, FP32 sums.
-  rmat_f16, fem_f16  the same with B in float16 (vcsr_spmm_f16).
-  rmat           2^22 R-MAT, O = 256: A cut into N nnz-balanced row panels,
-                 B broadcast once: strong scaling.
+  rmat_bf16, fem_bf16, rmat_f16, fem_f16  B held in bfloat16 / float16,
+                 widened to FP32 as it is loaded, FP32 sums.
 
 `--impl reference` times the reference's CSR algorithm (src/kernels.cu:15-33,
 restated in oracle/oracle.c) on the host cores instead, on rank 0 only.
@@ -39,9 +43,11 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "vcsr-spmm_b200"))
 
 METRIC = "SpMM GFLOP/s (2*nnz*O/t)"
+L2_NOTE = "flushed before every timed GPU step (256 MB write)"
 
 WORKLOADS = {
     # name: (generator config, size_param, O, scaling, label)
+    "rmat": ("rmat", 22, 256, "strong", "rmat_s22_O256"),
     "fem": ("fem", 0, 128, "weak", "fem_banded_62451_O128"),
     "fem_o32": ("fem", 0, 32, "weak", "fem_banded_62451_O32"),
     "fem_o512": ("fem", 0, 512, "weak", "fem_banded_62451_O512"),
@@ -50,7 +56,6 @@ WORKLOADS = {
     "powerlaw_o64": ("powerlaw", 0, 64, "weak", "powerlaw_321821_O64"),
     "blockdense": ("blockdense", 0, 512, "weak", "blockdense_65536_O512_fp32"),
     "blockdense_tf32": ("blockdense", 0, 512, "weak", "blockdense_65536_O512_tf32"),
-    "rmat": ("rmat", 22, 256, "strong", "rmat_s22_O256"),
     "rmat_bf16": ("rmat", 22, 256, "strong", "rmat_s22_O256_bf16in"),
     "fem_bf16": ("fem", 0, 128, "weak", "fem_banded_62451_O128_bf16in"),
     "rmat_f16": ("rmat", 22, 256, "strong", "rmat_s22_O256_f16in"),
@@ -66,10 +71,10 @@ HALF_WORKLOADS = {"rmat_bf16": "bfloat16", "fem_bf16": "bfloat16",
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="fem")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="rmat")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--size", type=int, default=None,
                     help="override the workload's size parameter (rows, or the R-MAT "
@@ -77,6 +82,11 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-peers", action="store_true")
+    ap.add_argument("--no-fem-record", action="store_true",
+                    help="leave out the FEM O=128 sub-record of the N=1 R-MAT line")
+    ap.add_argument("--sub-steps", type=int, default=400,
+                    help="timed steps of the FEM sub-record (short steps: a window "
+                         "long enough for the clock sampler)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="CPU baseline sample length")
     return ap.parse_args()
@@ -107,27 +117,37 @@ def profile_traffic(label):
     return None
 
 
+def cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 class Clocks:
-    """SM clock and clock-event reasons of one GPU, sampled through NVML by a
-    child process (so the benchmark's own thread never delays it) as fast as
-    NVML answers; only samples inside [start, stop] count (or the one just
-    before start, when the timed region is shorter than a sample)."""
+    """SM clock and clock-event reasons of one GPU, sampled through NVML about
+    every millisecond by a child process (so the benchmark's own thread never
+    delays it), written to a file; only samples inside [start, stop] count
+    (or the one just before start, when the timed region is shorter)."""
     CHILD = r"""
-import sys, time
+import select, sys, time
 import pynvml as N
 N.nvmlInit()
 h = N.nvmlDeviceGetHandleByUUID(sys.argv[1])
+out = open(sys.argv[2], "w")
 print("max", N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM), flush=True)
-import select
 while True:
-    r, _, _ = select.select([sys.stdin], [], [], 0)
+    r, _, _ = select.select([sys.stdin], [], [], 0.001)
     if r and not sys.stdin.readline():
         break
     t = time.monotonic()
     c = N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM)
     e = N.nvmlDeviceGetCurrentClocksEventReasons(h)
-    print(f"{t:.6f} {c} {e}", flush=False)
-sys.stdout.flush()
+    out.write(f"{t:.6f} {c} {e}\n")
+out.close()
 """
     REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
                0x40: "hw_thermal_slowdown"}
@@ -135,19 +155,24 @@ sys.stdout.flush()
     def __init__(self, uuid):
         self.uuid = uuid
         self.proc = None
+        self.path = None
         self.t0 = self.t1 = None
         self.max_mhz = None
 
     def launch(self):
         import subprocess
+        import tempfile
         try:
-            self.proc = subprocess.Popen([sys.executable, "-c", self.CHILD, self.uuid],
+            fd, self.path = tempfile.mkstemp(prefix="clocks", suffix=".txt")
+            os.close(fd)
+            self.proc = subprocess.Popen([sys.executable, "-c", self.CHILD, self.uuid, self.path],
                                          stdin=subprocess.PIPE, stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
             first = self.proc.stdout.readline().split()
             self.max_mhz = float(first[1]) if len(first) == 2 else None
         except Exception:
             self.proc = None
+        return self
 
     def start(self):
         self.t0 = time.monotonic()
@@ -156,14 +181,17 @@ sys.stdout.flush()
         self.t1 = time.monotonic()
         if self.proc is None:
             return None
-        time.sleep(0.002)
+        time.sleep(0.003)
         try:
-            out, _ = self.proc.communicate(input="\n", timeout=30)
+            self.proc.communicate(input="\n", timeout=30)
+            with open(self.path) as f:
+                lines = f.read().splitlines()
+            os.unlink(self.path)
         except Exception:
             self.proc.kill()
             return None
         samples = []
-        for line in out.splitlines():
+        for line in lines:
             f = line.split()
             if len(f) == 3:
                 samples.append((float(f[0]), float(f[1]), int(f[2])))
@@ -179,56 +207,83 @@ sys.stdout.flush()
         return {"sm_mhz": float(np.median([x[1] for x in inside])),
                 "sm_max_mhz": self.max_mhz,
                 "reasons": sorted(v for k, v in self.REASONS.items() if reasons & k),
-                "samples": len(inside), "source": "nvml",
+                "samples": len(inside), "source": "nvml, ~1 ms interval",
                 "window_ms": round((self.t1 - self.t0) * 1e3, 3)}
 
 
 def algorithmic_bytes(csr, O, b_bytes=4):
+    """A as CSR (values + indices + row pointers), B after perfect reuse (each
+    touched row once), C written once."""
     touched = int(np.count_nonzero(np.bincount(csr.col, minlength=csr.N))) if csr.nnz else 0
     return (8 * csr.nnz + 4 * (csr.M + 1) + b_bytes * O * touched + 4 * O * csr.M), touched
 
 
-def cpu_reference(csr, B, seconds, min_reps=3):
-    """The reference CSR algorithm on all host cores (oracle port)."""
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle
+def sample_rows(csr, O, flops_cap):
+    """Every k-th row of A, k chosen so that the sample holds at most about
+    flops_cap flops (all rows when A is small enough): a sample with the
+    matrix's own mix of short and long rows.  Returns (row_ptr, col, val,
+    rows, description)."""
+    total = 2.0 * csr.nnz * O
+    if total <= flops_cap:
+        return csr.row_ptr, csr.col, csr.val, csr.M, f"all {csr.M} rows"
+    k = int(np.ceil(total / flops_cap))
+    rows = np.arange(0, csr.M, k)
+    lens = (csr.row_ptr[rows + 1] - csr.row_ptr[rows]).astype(np.int64)
+    rp = np.zeros(len(rows) + 1, np.int64)
+    np.cumsum(lens, out=rp[1:])
+    idx = np.repeat(csr.row_ptr[rows].astype(np.int64) - rp[:-1], lens) + np.arange(rp[-1])
+    return (rp.astype(np.int32), csr.col[idx], csr.val[idx], len(rows),
+            f"every {k}th row ({len(rows)} of {csr.M} rows)")
+
+
+def host_threads():
     # every core this process may run on: torchrun sets OMP_NUM_THREADS=1 for
     # its ranks, which must not shrink the CPU arm
     try:
-        threads = len(os.sched_getaffinity(0))
+        return len(os.sched_getaffinity(0))
     except AttributeError:
-        threads = os.cpu_count() or oracle.max_threads()
-    M = csr.M
-    flops_full = 2.0 * csr.nnz * B.shape[1]
-    # bounded sample: leading rows holding at most ~2 GFLOP per repetition
-    rows = M
-    if flops_full > 2e9:
-        target = int(2e9 / (2.0 * B.shape[1]))
-        rows = int(np.searchsorted(csr.row_ptr, target))
-        rows = max(1, min(M, rows))
-    nnz_s = int(csr.row_ptr[rows])
-    Cm = np.empty((rows, B.shape[1]), np.float32)
-    rp, cc, vv = csr.row_ptr, csr.col, csr.val
+        return os.cpu_count() or 1
+
+
+def cpu_reference(csr, B, seconds, min_reps=3, threads=None, flops_cap=2e9):
+    """The reference CSR algorithm (src/kernels.cu:15-33, restated in the
+    oracle) on the host cores, over a bounded sample of rows."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    threads = threads or host_threads()
+    O = B.shape[1]
+    rp, cc, vv, rows, what = sample_rows(csr, O, flops_cap)
+    nnz_s = int(rp[rows])
+    Cm = np.empty((rows, O), np.float32)
     oracle.csr_spmm_f32_into(rows, rp, cc, vv, B, Cm, threads)  # warm-up
     reps, t0 = 0, time.perf_counter()
     while reps < min_reps or time.perf_counter() - t0 < seconds:
         oracle.csr_spmm_f32_into(rows, rp, cc, vv, B, Cm, threads)
         reps += 1
     dt = (time.perf_counter() - t0) / reps
-    gflops = 2.0 * nnz_s * B.shape[1] / dt / 1e9
-    sample = (f"rows [0,{rows}) of {M} ({nnz_s} of {csr.nnz} nnz), O={B.shape[1]}, "
+    gflops = 2.0 * nnz_s * O / dt / 1e9
+    sample = (f"{what}, {nnz_s} of {csr.nnz} nnz, O={O}, "
               f"{reps} reps x {dt * 1e3:.2f} ms")
     return {"value": round(gflops, 3), "unit": "GFLOP/s", "cores": threads,
             "kind": "port", "sample": sample}
 
 
-def build_inputs(args, rank, world):
-    from vcsr_b200 import dist as D
-    cfg, size, O, scaling, label = WORKLOADS[args.workload]
-    if args.size is not None:
-        size, label = args.size, f"{label}@size{args.size}"
-    csr, row0, total = D.rank_panel(cfg, size, args.seed, rank, world, scaling, align=16)
-    return csr, O, scaling, label, total
+def cpu_baseline(csr, B, seconds):
+    """All host threads, plus the same algorithm on one thread (a smaller
+    sample) and the host CPU model."""
+    allc = cpu_reference(csr, B, seconds)
+    one = cpu_reference(csr, B, min(3.0, seconds / 3), min_reps=1, threads=1, flops_cap=2e8)
+    allc["single_thread"] = {"value": one["value"], "unit": "GFLOP/s", "cores": 1,
+                             "sample": one["sample"]}
+    allc["cpu_model"] = cpu_model()
+    return allc
+
+
+def workload_config(label, csr_M, csr_N, global_nnz, O, world):
+    """The workload's description, the same in both arms (no plan details)."""
+    return {"workload": label, "M": csr_M, "N": csr_N, "global_nnz": global_nnz, "O": O,
+            "segw": 4, "bundle": 32, "l2": L2_NOTE,
+            "parallelism": (f"row panels x{world}, B broadcast once" if world > 1 else "1 GPU")}
 
 
 def run_reference(args):
@@ -251,44 +306,100 @@ def run_reference(args):
         vals.append(info["value"])
     v = float(np.median(vals))
     flops = 2.0 * csr.nnz * O
+    world = args.gpus
     line = {"metric": METRIC, "value": round(v, 3), "unit": "GFLOP/s",
-            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(flops / (v * 1e9) * 1e3, 4),
             "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
             "dtype": "f32", "data": "synthetic", "impl": "reference",
-            "config": {"workload": label, "nnz": csr.nnz, "O": O,
-                       "algorithm": "reference CSR SpMM (src/kernels.cu:15-33) "
-                                    "on host cores, OpenMP over rows"},
-            "cpu_baseline": dict(info, value=round(v, 3)),
+            "config": workload_config(label, csr.M, csr.N, csr.nnz, O, world),
+            "algorithm": "reference CSR SpMM (src/kernels.cu:15-33) on host cores, "
+                         "OpenMP over rows",
+            "cpu_baseline": dict(info, value=round(v, 3), cpu_model=cpu_model()),
             "e2e": {"value": round(v, 3), "unit": "GFLOP/s",
                     "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
-def run_ours(args):
-    import torch
-    import torch.distributed as dist
-    import vcsr_b200 as V
+def timed_events(torch, fn, n, stream, flush):
+    """Per-call device times (ms) of fn over n calls, L2 flushed before each."""
+    ts = []
+    for _ in range(n):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        fn()
+        b.record(stream)
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b))
+    return ts
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if not torch.cuda.is_available():
-        raise SystemExit("bench.py needs a CUDA GPU (no CPU fallback)")
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=dev)
-    stream = torch.cuda.current_stream()
 
-    from vcsr_b200 import dist as D
-    csr, O, scaling, label, strong_total = build_inputs(args, rank, world)
-    global_nnz = D.global_nnz(csr, scaling, world, strong_total,
-                              dist if world > 1 else None, dev)
-    lo = 0.0 if WORKLOADS[args.workload][0] == "rmat" else -1.0
-    tf32 = args.workload in TF32_WORKLOADS
+def library_peers(torch, V, csr, dB32, O, dC, flush, stream, flops, value, reps):
+    """cuSPARSE (best of its CSR algorithms, handle and preprocessing outside
+    the timed call) and the engine's own CSR row-wise kernel, same B200."""
+    peers = {}
+    d = V.DeviceCSR(csr)
+    dCp = torch.empty_like(dC)
+    best = None
+    for alg in (0, 1, 2, 3):
+        try:
+            h = V.CuSparse(d, dB32, O, dCp, alg=alg)
+        except V.VcsrError:
+            continue
+        for _ in range(3):
+            flush.zero_()
+            h.run()
+        ts = timed_events(torch, h.run, reps, stream, flush)
+        h.close()
+        g = flops / (np.mean(ts) * 1e-3) / 1e9
+        if best is None or g > best[1]:
+            best = (V.CuSparse.ALGS[alg], g)
+    if best:
+        peers["cusparse_best"] = {"alg": best[0], "gflops": round(best[1], 2),
+                                  "ours_over_cusparse": round(value / best[1], 3)}
+    ts = timed_events(torch, lambda: V.run_csr_spmm_gpu(csr.M, d.row_ptr, d.col, d.val, dB32,
+                                                        O, dCp, stream), reps, stream, flush)
+    peers["csr_rowwise_gflops"] = round(flops / (np.mean(ts) * 1e-3) / 1e9, 2)
+    del d, dCp
+    return peers
+
+
+def reference_gpu_peers(torch, V, csr, dB32, O, flush, stream, flops, reps):
+    """The reference's own kernels rebuilt for sm_100a (baseline/_ref, built
+    from the reference tree by baseline/Makefile), each on the input it
+    takes, its own event timing around the kernel alone: csr_spmm_kernel
+    (src/kernels.cu:15-33), vcsr_spmm_kernel (src/kernels.cu:37-103),
+    vcsr_opt_kernel (src/vcsr_opt.cu:115-241), vcsr_seg_prefetch_kernel
+    (src/vcsr_seg.cu:124-189) and aspt_spmm_kernel (src/aspt.cu:38-142).
+    The VCSR kernels read the segment-major format built by the engine's GPU
+    builder (bit-exact with the reference's builder up to tie order); the
+    segment kernels read whole segments of B, so B gets segw padding rows."""
+    sys.path.insert(0, os.path.join(ROOT, "baseline"))
+    try:
+        import ref_gpu
+    except Exception as e:  # not built here
+        return {"unavailable": f"baseline/_ref not built ({type(e).__name__}: {e})"}
+    try:
+        return ref_gpu.time_all(torch, V, csr, dB32, O, flush, stream, flops, reps)
+    except Exception as e:
+        return {"unavailable": f"{type(e).__name__}: {e}"}
+
+
+def measure(args, ctx, workload, steps, warmup, extras):
+    """One workload: plan, B (broadcast under N ranks), `steps` timed steps,
+    and (extras) the roofline, peers, end-to-end figure and CPU baseline."""
+    torch, V, D, dist = ctx["torch"], ctx["V"], ctx["D"], ctx["dist"]
+    rank, world, dev, stream = ctx["rank"], ctx["world"], ctx["dev"], ctx["stream"]
+    cfg, size, O, scaling, label = WORKLOADS[workload]
+    if args.size is not None and workload == args.workload:
+        size, label = args.size, f"{label}@size{args.size}"
+    dd = dist if world > 1 else None
+    csr, row0, strong_total = D.rank_panel(cfg, size, args.seed, rank, world, scaling, align=16)
+    global_nnz = D.global_nnz(csr, scaling, world, strong_total, dd, dev)
+    global_M = D.sum_over_ranks(dist, csr.M, dev) if world > 1 else csr.M
+    lo = 0.0 if cfg == "rmat" else -1.0
+    tf32 = workload in TF32_WORKLOADS
     plan = V.Plan(csr, segw=4, bundle=32, max_O=max(O, 512), tf32_panels=tf32, target_O=O)
     info = plan.info()
 
@@ -297,15 +408,14 @@ def run_ours(args):
     bcast_ms = None
     if rank == 0 or world == 1:
         V.gen_dense_device(dB, args.seed + 1000, lo, 1.0)
-    half = HALF_WORKLOADS.get(args.workload)
-    bf16 = half is not None  # any 16-bit B
+    half = HALF_WORKLOADS.get(workload)
     dB32 = dB  # FP32 copy for the peers and the CPU baseline
-    if bf16:
+    if half:
         dB32 = dB.to(getattr(torch, half)).float()  # the values the 16-bit path sees
         dB = dB.to(getattr(torch, half))
     if world > 1:
         torch.cuda.synchronize()
-        if bf16:
+        if half:
             D.broadcast_b(dist, dB32, 0)
         D.broadcast_b(dist, dB, 0)  # first collective on this buffer: NCCL set-up
         torch.cuda.synchronize()
@@ -317,19 +427,13 @@ def run_ours(args):
         torch.cuda.synchronize()
         bcast_ms = D.max_over_ranks(dist, e0.elapsed_time(e1), dev)
     dC = torch.empty(csr.M, O, device=dev)
-    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)  # 256 MB
+    flush = ctx["flush"]
 
     def step():
         plan.spmm(dB, dC, stream=stream)
 
-    try:
-        uuid = str(torch.cuda.get_device_properties(dev).uuid)
-        gpu_id = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
-    except Exception:
-        gpu_id = ""
-    clocks = Clocks(gpu_id)
-    clocks.launch()
-    for _ in range(args.warmup):
+    clocks = Clocks(ctx["gpu_id"]).launch()
+    for _ in range(warmup):
         flush.zero_()
         step()
     torch.cuda.synchronize()
@@ -337,10 +441,10 @@ def run_ours(args):
         dist.barrier()
     torch.cuda.synchronize()
     clocks.start()
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     launches = 0
-    for i in range(args.steps):
+    for i in range(steps):
         flush.zero_()
         starts[i].record(stream)
         step()
@@ -353,12 +457,12 @@ def run_ours(args):
     clk = clocks.stop()
     per = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     total_ms = D.max_over_ranks(dist, sum(per), dev) if world > 1 else sum(per)
-    ms_step = total_ms / args.steps
+    ms_step = total_ms / steps
     flops_step = 2.0 * global_nnz * O
     value = flops_step / (ms_step * 1e-3) / 1e9
 
-    # roofline of the dominant (only) kernel, per launch, on this rank
-    abytes, touched = algorithmic_bytes(csr, O, 2 if bf16 else 4)
+    # roofline of the dominant kernel, per launch, on this rank
+    abytes, touched = algorithmic_bytes(csr, O, 2 if half else 4)
     avg_ms = float(np.mean(per))
     achieved = abytes / (avg_ms * 1e-3) / 1e9
     peak, peak_kind = peaks()
@@ -377,12 +481,48 @@ def run_ours(args):
                 "peak_tflops": round(fpk, 1),
                 "peak_kind": "nominal: SMs x 128 FP32 lanes x 2 x max SM clock",
                 "frac_useful": round(useful / fpk, 4), "frac_slots": round(slots / fpk, 4)}
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "traffic": traffic,
+                "peak_kind": peak_kind, "algorithmic_bytes": int(abytes),
+                "kernel_ms": round(avg_ms, 5), "fp32_fma": fp32}
+    plan_info = {"vec_rows": info["vec_rows"], "units": info["num_units"],
+                 "split_units": info["num_split_units"], "long_units": info["num_long_units"],
+                 "cols_touched": touched, "tf32_panel_blocks": info["num_panel_blocks"],
+                 "tf32_panel_nnz": info["panel_nnz"], "build_ms": round(info["build_ms"], 1)}
 
-    # several GPUs: B's broadcast overlapped with the product (row panels
-    # multiplied as their chunk of B arrives), timed like the step: max over
-    # ranks of the device time of broadcast + product
-    fused_ms = None
-    if world > 1 and not bf16:
+    rec = {"value": round(value, 3), "ms_per_step": round(ms_step, 5),
+           "config": workload_config(label, global_M, csr.N, global_nnz, O, world),
+           "scaling": scaling, "plan": plan_info, "roofline": roofline,
+           "gpu_launches": int(launches), "clocks": clk,
+           "dtype": "tf32" if tf32 else ((({"bfloat16": "bf16", "float16": "f16"}[half])
+                                          + "-in/f32-acc") if half else "f32")}
+    if world > 1:
+        # every rank's panel, kernel time and roofline; the limiter of the curve
+        mine = {"rank": rank, "rows": csr.M, "nnz": csr.nnz, "cols_touched": touched,
+                "kernel_ms": round(avg_ms, 5), "roofline_frac": round(achieved / peak, 4),
+                "achieved_gbs": round(achieved, 1), "split_units": info["num_split_units"],
+                "long_units": info["num_long_units"], "build_ms": round(info["build_ms"], 1)}
+        ranks = [None] * world
+        dist.all_gather_object(ranks, mine)
+        kms = [r["kernel_ms"] for r in ranks]
+        slow = int(np.argmax(kms))
+        imb = max(kms) / max(1e-9, float(np.mean(kms)))
+        rec["ranks"] = ranks
+        rec["bcast_ms"] = round(bcast_ms, 4)
+        rec["bcast_bytes"] = int(csr.N * O * (2 if half else 4))
+        if imb > 1.15:
+            lim = (f"row-panel imbalance: rank {slow} takes {max(kms):.3f} ms against a mean of "
+                   f"{np.mean(kms):.3f} ms")
+        else:
+            lim = (f"per-rank kernel time (panels within {100 * (imb - 1):.0f}% of the mean; "
+                   f"slowest rank {slow})")
+        rec["limiter"] = lim + (f"; the one-time B broadcast ({bcast_ms:.2f} ms) is "
+                                f"{bcast_ms / ms_step:.1f} steps")
+
+    if extras and world > 1 and not half:
+        # B's broadcast overlapped with the product (row panels multiplied as
+        # their chunk of B arrives), timed like the step: max over ranks of
+        # the device time of broadcast + product
         ts = []
         for i in range(4):
             dist.barrier()
@@ -394,114 +534,92 @@ def run_ours(args):
             torch.cuda.synchronize()
             if i > 0:
                 ts.append(D.max_over_ranks(dist, e0.elapsed_time(e1), dev))
-        fused_ms = float(np.median(ts))
+        rec["bcast_overlapped_ms"] = round(float(np.median(ts)), 4)
 
     # end to end through the host-buffer entry point (pinned buffers)
-    e2e = None
-    if not args.no_e2e and not bf16:  # the host-buffer entry point takes FP32 B
+    if extras and not args.no_e2e and not half:  # the host-buffer entry point takes FP32 B
         hB = torch.empty(csr.N, O, dtype=torch.float32, pin_memory=True)
         hB.copy_(dB32.cpu())
         hC = torch.empty(csr.M, O, dtype=torch.float32, pin_memory=True)
-        for _ in range(max(3, min(5, args.warmup))):
+        for _ in range(max(3, min(5, warmup))):
             plan.spmm_host(hB.numpy(), hC.numpy(), stream=stream)
         if world > 1:
             dist.barrier()
-        n_e2e = max(5, min(args.steps, 20))
+        n_e2e = max(5, min(steps, 20))
         t0 = time.perf_counter()
         for _ in range(n_e2e):
             plan.spmm_host(hB.numpy(), hC.numpy(), stream=stream)
-        dt = torch.tensor([(time.perf_counter() - t0) / n_e2e], device=dev,
-                          dtype=torch.float64)
+        dt = (time.perf_counter() - t0) / n_e2e
         if world > 1:
-            dist.all_reduce(dt, op=dist.ReduceOp.MAX)
-        e2e = {"value": round(flops_step / float(dt.item()) / 1e9, 3), "unit": "GFLOP/s",
-               "h2d_bytes_per_step": int(csr.N * O * 4 * world),
-               "d2h_bytes_per_step": int(csr.M * O * 4 * world),
-               "ms_per_step": round(float(dt.item()) * 1e3, 4),
-               "api": "vcsr_spmm_host (pinned host B and C)"}
+            dt = D.max_over_ranks(dist, dt, dev)
+        rec["e2e"] = {"value": round(flops_step / dt / 1e9, 3), "unit": "GFLOP/s",
+                      "h2d_bytes_per_step": int(csr.N * O * 4 * world),
+                      "d2h_bytes_per_step": int(global_M * O * 4),
+                      "ms_per_step": round(dt * 1e3, 4),
+                      "api": "vcsr_spmm_host (pinned host B and C)"}
+        del hB, hC
 
-    peers = None
-    if not args.no_peers and world == 1:
-        peers = {}
-        d = V.DeviceCSR(csr)
-        dCp = torch.empty_like(dC)
-        best = None
-        for alg in (0, 1, 2, 3):
-            try:
-                h = V.CuSparse(d, dB32, O, dCp, alg=alg)
-            except V.VcsrError:
-                continue
-            for _ in range(3):
-                flush.zero_()
-                h.run()
-            ts = []
-            for _ in range(max(5, min(args.steps, 20))):
-                flush.zero_()
-                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                a.record(stream)
-                h.run()
-                b.record(stream)
-                torch.cuda.synchronize()
-                ts.append(a.elapsed_time(b))
-            h.close()
-            g = flops_step / (np.mean(ts) * 1e-3) / 1e9
-            if best is None or g > best[1]:
-                best = (V.CuSparse.ALGS[alg], g)
-        if best:
-            peers["cusparse_best"] = {"alg": best[0], "gflops": round(best[1], 2),
-                                      "ours_over_cusparse": round(value / best[1], 3)}
-        ts = []
-        for _ in range(max(5, min(args.steps, 20))):
-            flush.zero_()
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record(stream)
-            V.run_csr_spmm_gpu(csr.M, d.row_ptr, d.col, d.val, dB32, O, dCp, stream)
-            b.record(stream)
-            torch.cuda.synchronize()
-            ts.append(a.elapsed_time(b))
-        peers["csr_rowwise_gflops"] = round(flops_step / (np.mean(ts) * 1e-3) / 1e9, 2)
+    if extras and not args.no_peers and world == 1:
+        reps = max(5, min(steps, 20))
+        rec["peers"] = library_peers(torch, V, csr, dB32, O, dC, flush, stream, flops_step,
+                                     value, reps)
+        rec["peers"]["reference_kernels_sm100a"] = reference_gpu_peers(
+            torch, V, csr, dB32, O, flush, stream, flops_step, min(reps, 5))
+    if extras and rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rec["cpu_baseline"] = cpu_baseline(csr, dB32.cpu().numpy(), args.cpu_seconds)
+    del plan, dB, dB32, dC
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return rec
 
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        B = dB32.cpu().numpy()
-        cpu = cpu_reference(csr, B, args.cpu_seconds)
 
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    import vcsr_b200 as V
+    from vcsr_b200 import dist as D
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA GPU (no CPU fallback)")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        D.init_ranks(dist, "nccl", timeout_s=300, device=dev)
+    try:
+        uuid = str(torch.cuda.get_device_properties(dev).uuid)
+        gpu_id = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+    except Exception:
+        gpu_id = ""
+    ctx = {"torch": torch, "V": V, "D": D, "dist": dist, "rank": rank, "world": world,
+           "dev": dev, "stream": torch.cuda.current_stream(), "gpu_id": gpu_id,
+           "flush": torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)}  # 256 MB
+    main = measure(args, ctx, args.workload, args.steps, args.warmup, extras=True)
+    sub = None
+    if world == 1 and args.workload == "rmat" and not args.no_fem_record and args.size is None:
+        sub = measure(args, ctx, "fem", max(args.steps, args.sub_steps), args.warmup,
+                      extras=True)
+        sub["steps"] = max(args.steps, args.sub_steps)
     if world > 1:
         dist.barrier()
     if rank == 0:
-        line = {
-            "metric": METRIC, "value": round(value, 3), "unit": "GFLOP/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(ms_step, 5), "higher_is_better": True,
-            "scaling": scaling, "vs_baseline": None, "dtype": "tf32" if tf32 else ({"bfloat16": "bf16", "float16": "f16"}[half] + "-in/f32-acc" if bf16 else "f32"),
-            "data": "synthetic",
-            "config": {"workload": label, "M": csr.M, "N": csr.N, "nnz": csr.nnz,
-                       "global_nnz": global_nnz, "O": O, "segw": 4, "bundle": 32,
-                       "vec_rows": info["vec_rows"], "units": info["num_units"],
-                       "split_units": info["num_split_units"],
-                       "cols_touched": touched,
-                       "tf32_panel_blocks": info["num_panel_blocks"],
-                       "tf32_panel_nnz": info["panel_nnz"],
-                       "l2": "flushed before every timed step (256 MB write)",
-                       "parallelism": (f"row panels x{world}, B broadcast once"
-                                       if world > 1 else "1 GPU")},
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1),
-                         "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": traffic,
-                         "peak_kind": peak_kind,
-                         "algorithmic_bytes": int(abytes),
-                         "kernel_ms": round(avg_ms, 5), "fp32_fma": fp32},
-            "gpu_launches": int(launches),
-            "e2e": e2e, "clocks": clk, "cpu_baseline": cpu, "peers": peers,
-            "build_ms": round(info["build_ms"], 1),
-        }
-        if bcast_ms is not None:
-            line["bcast_ms"] = round(bcast_ms, 4)
-        if fused_ms is not None:
-            line["bcast_overlapped_ms"] = round(fused_ms, 4)  # broadcast + product together
-            line["bcast_bytes"] = int(csr.N * O * 4)
+        line = {"metric": METRIC, "value": main["value"], "unit": "GFLOP/s",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": main["ms_per_step"], "higher_is_better": True,
+                "scaling": main["scaling"], "vs_baseline": None, "dtype": main["dtype"],
+                "data": "synthetic", "config": main["config"],
+                "roofline": main["roofline"], "gpu_launches": main["gpu_launches"],
+                "e2e": main.get("e2e"), "clocks": main["clocks"],
+                "cpu_baseline": main.get("cpu_baseline"), "peers": main.get("peers"),
+                "plan": main["plan"]}
+        for k in ("ranks", "bcast_ms", "bcast_bytes", "bcast_overlapped_ms", "limiter"):
+            if k in main:
+                line[k] = main[k]
+        if sub is not None:
+            line["fem_o128"] = sub
         print(json.dumps(line), flush=True)
-    del plan
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -175,6 +175,10 @@ typedef struct vcsr_plan vcsr_plan;
  * Needs O and ldb multiples of 4 and a 16-byte aligned B at call time
  * (VCSR_ERR_UNSUPPORTED otherwise). */
 #define VCSR_PLAN_TF32_PANELS 2
+/* Build the plan's layout on the host (OpenMP) instead of with the GPU
+ * kernels that build it by default.  The layout is the same, bit for bit;
+ * the flag exists to check the GPU builder against the host one. */
+#define VCSR_PLAN_HOST_BUILD 4
 
 typedef struct vcsr_plan_params {
   int segw;     /* column segment width (--segw) */

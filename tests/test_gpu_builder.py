@@ -1,0 +1,115 @@
+"""The plan's layout built by GPU kernels (the default) against the host
+builder (VCSR_PLAN_HOST_BUILD): bit-identical, compared through the saved
+plan files (every array of the layout, the row panels and the dense TF32
+panels; the build flag itself is not saved).  Cases: the five benchmark
+configurations (scaled, and the full FEM and power-law matrices), every
+vector height, TF32 panels, unsorted rows with duplicates, empty rows, small
+chunks that split vectors, and the empty matrix.  The GPU-built plan's
+product is also checked against the oracle, and bad inputs are refused as
+the host builder refuses them.
+"""
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+import vcsr_b200 as V
+from helpers import random_csr, rel_l2
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+
+def same_layout(tmp_path, csr, **kw):
+    a = V.Plan(csr, **kw)
+    b = V.Plan(csr, host_build=True, **kw)
+    pa, pb = os.path.join(tmp_path, "gpu.plan"), os.path.join(tmp_path, "host.plan")
+    a.save(pa)
+    b.save(pb)
+    ia, ib = a.info(), b.info()
+    for k in ia:
+        if k != "build_ms":
+            assert ia[k] == ib[k], (k, ia[k], ib[k])
+    assert a.row_panels() == b.row_panels()
+    with open(pa, "rb") as f:
+        ga = f.read()
+    with open(pb, "rb") as f:
+        gb = f.read()
+    assert ga == gb, "layouts differ"
+    return a
+
+
+@pytest.mark.parametrize("cfg,size,kw", [
+    ("uniform", 0, {}),
+    ("fem", 6000, {}),
+    ("fem", 6000, {"target_O": 512}),
+    ("fem", 3001, {"vec_rows": 2}),
+    ("fem", 3001, {"vec_rows": 16}),
+    ("powerlaw", 60000, {}),
+    ("rmat", 16, {}),
+    ("blockdense", 2048, {}),
+    ("blockdense", 2048, {"chunk": 256}),
+    ("blockdense", 2048, {"tf32_panels": True}),
+    ("blockdense", 1008, {"tf32_panels": True, "panel_min_nnz": 40}),
+    ("fem", 0, {}),
+    ("powerlaw", 0, {}),
+])
+def test_gpu_layout_equals_host_layout(tmp_path, cfg, size, kw):
+    csr = V.gen_csr(cfg, 0, size)
+    plan = same_layout(tmp_path, csr, **kw)
+    O = 64
+    B = V.gen_dense_host(csr.N, O, 3)
+    dC = torch.empty(csr.M, O, device="cuda")
+    plan.spmm(torch.from_numpy(B).cuda(), dC)
+    plan.check()
+    ref = oracle.csr_spmm_f64(csr.M, csr.row_ptr, csr.col, csr.val, B)
+    tol = 2e-3 if kw.get("tf32_panels") else 1e-5
+    assert rel_l2(dC.cpu().numpy(), ref) <= tol
+
+
+@pytest.mark.parametrize("R", [0, 1, 2, 4, 8])
+def test_unsorted_rows_with_duplicates(tmp_path, R):
+    rp, col, val = random_csr(7, 700, 900, 0.03, dup_rows=range(0, 700, 5),
+                              dense_rows=(3, 400), unsorted=True)
+    csr = V.CSR(700, 900, len(val), rp, col, val)
+    plan = same_layout(tmp_path, csr, vec_rows=R)
+    B = V.gen_dense_host(900, 32, 4)
+    dC = torch.empty(700, 32, device="cuda")
+    plan.spmm(torch.from_numpy(B).cuda(), dC)
+    torch.cuda.synchronize()
+    ref = oracle.csr_spmm_f32(700, rp, col, val, B)  # CSR order = the input order, sorted stably
+    assert rel_l2(dC.cpu().numpy(), ref) <= 1e-5
+
+
+def test_device_csr_input_and_empty_cases(tmp_path):
+    csr = V.gen_csr("fem", 1, 5000)
+    a = V.Plan(V.DeviceCSR(csr))
+    b = V.Plan(csr, host_build=True)
+    pa, pb = os.path.join(tmp_path, "a"), os.path.join(tmp_path, "b")
+    a.save(pa)
+    b.save(pb)
+    assert open(pa, "rb").read() == open(pb, "rb").read()
+    rp = np.zeros(51, np.int32)  # 50 empty rows
+    same_layout(tmp_path, V.CSR(50, 10, 0, rp, np.zeros(0, np.int32), np.zeros(0, np.float32)))
+    same_layout(tmp_path, V.CSR(0, 10, 0, np.zeros(1, np.int32), np.zeros(0, np.int32),
+                                np.zeros(0, np.float32)))
+
+
+def test_bad_inputs_refused_like_the_host_builder():
+    rp = np.array([0, 2, 1, 3], np.int32)
+    col = np.array([0, 1, 2], np.int32)
+    val = np.ones(3, np.float32)
+    for host in (False, True):
+        with pytest.raises(V.VcsrError) as ei:
+            V.Plan(V.CSR(3, 4, 3, rp, col, val), host_build=host)
+        assert ei.value.status == 1 and "decreases at row 1" in ei.value.msg
+        with pytest.raises(V.VcsrError) as ei:
+            V.Plan(V.CSR(2, 2, 3, np.array([0, 1, 3], np.int32), col, val), host_build=host)
+        assert ei.value.status == 8 and "column 2 of entry 2" in ei.value.msg
+
+
+def test_full_rmat_gpu_layout_equals_host_layout(tmp_path):
+    csr = V.gen_csr("rmat", 0, 22)
+    a = same_layout(tmp_path, csr, max_O=256, target_O=256)
+    assert a.info()["build_ms"] < 1000

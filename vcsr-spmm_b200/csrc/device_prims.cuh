@@ -4,30 +4,39 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <vector>
 
 #include "common.h"
 
 namespace vcsr {
 
-// Stream-ordered device scratch; every allocation is released together.
+// Stream-ordered device scratch; every allocation is released together (or
+// earlier with release()).
 struct Scratch {
   cudaStream_t st;
-  void *ptrs[64];
-  int n = 0;
+  std::vector<void *> ptrs;
   explicit Scratch(cudaStream_t s) : st(s) {}
   ~Scratch() {
-    for (int i = 0; i < n; ++i) cudaFreeAsync(ptrs[i], st);
+    for (void *p : ptrs) cudaFreeAsync(p, st);
   }
   template <class T>
   vcsr_status get(T **out, int64_t count) {
-    if (n == 64) return fail(VCSR_ERR_ALLOC, "scratch table full");
     size_t bytes = sizeof(T) * (size_t)(count > 0 ? count : 1);
     cudaError_t e = cudaMallocAsync((void **)out, bytes, st);
     if (e != cudaSuccess)
       return fail(VCSR_ERR_ALLOC, "device scratch of %zu bytes: %s", bytes,
                   cudaGetErrorString(e));
-    ptrs[n++] = *out;
+    ptrs.push_back(*out);
     return VCSR_OK;
+  }
+  // frees one allocation now (stream-ordered)
+  void release(void *p) {
+    for (size_t i = 0; i < ptrs.size(); ++i)
+      if (ptrs[i] == p) {
+        cudaFreeAsync(p, st);
+        ptrs.erase(ptrs.begin() + (long)i);
+        return;
+      }
   }
 };
 

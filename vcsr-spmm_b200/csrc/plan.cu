@@ -14,6 +14,7 @@
 
 #include "common.h"
 #include "panel.h"
+#include "panel_gpu.h"
 #include "plan_impl.h"
 #include "panel_tc.h"
 #include "spmm_kernels.h"
@@ -162,6 +163,37 @@ vcsr_status host_sorted_csr(const vcsr_csr *in, int where, vcsr_csr *out,
   return VCSR_OK;
 }
 
+// The default build: the CSR goes to (or stays on) the device, is validated
+// and, if needed, row-sorted there, and every array of the layout is built
+// by device kernels (panel_gpu_build.cu); the host reads back only totals.
+vcsr_status create_on_device(vcsr_plan *p, const vcsr_csr *csr, int where, int sms,
+                             cudaStream_t st) {
+  vcsr_csr din = *csr, up{}, sorted{};
+  bool up_owned = false, sorted_owned = false;
+  vcsr_status s = VCSR_OK;
+  int zero = 0;
+  if (where == VCSR_HOST || csr->M == 0) {  // to the device (M = 0: a valid row_ptr)
+    vcsr_csr h = *csr;
+    if (csr->M == 0) h.row_ptr = &zero;
+    s = vcsr_csr_to_device(&h, &up, st);
+    up_owned = s == VCSR_OK;
+    din = up;
+  }
+  if (s == VCSR_OK) s = vcsr::device_sorted_csr(din, &sorted, &sorted_owned, st);
+  if (s == VCSR_OK) s = vcsr::build_plan_layout_device(p, sorted, sms, st);
+  if (s == VCSR_OK) s = vcsr::plan_finish(p, st);
+  if (s == VCSR_OK && (p->params.flags & VCSR_PLAN_REFERENCE_FORMAT)) {
+    s = vcsr_build_vcsr(&sorted, p->params.segw, p->params.bundle, &p->ref, st);
+    p->has_ref = s == VCSR_OK;
+  }
+  const cudaError_t e = cudaStreamSynchronize(st);  // the temporaries die here
+  if (sorted_owned) vcsr_csr_free(&sorted, VCSR_DEVICE);
+  if (up_owned) vcsr_csr_free(&up, VCSR_DEVICE);
+  if (s != VCSR_OK) return s;
+  if (e != cudaSuccess) return fail(VCSR_ERR_CUDA, "plan build: %s", cudaGetErrorString(e));
+  return VCSR_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -204,6 +236,18 @@ vcsr_status vcsr_plan_create(const vcsr_csr *csr, int csr_where,
     cudaGetDevice(&p->device);
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, p->device);
+    if (!(params->flags & VCSR_PLAN_HOST_BUILD)) {  // the layout built by GPU kernels
+      const vcsr_status s = create_on_device(p, csr, csr_where, sms, st);
+      if (s != VCSR_OK) {
+        vcsr::plan_release(p);
+        delete p;
+        return s;
+      }
+      p->build_ms = std::chrono::duration<double, std::milli>(
+                        std::chrono::steady_clock::now() - t0).count();
+      *out = p;
+      return VCSR_OK;
+    }
 
     vcsr_csr h{};
     bool owned = false;
@@ -275,9 +319,11 @@ vcsr_status vcsr_plan_create(const vcsr_csr *csr, int csr_where,
     // Split parts and units of at least kLongUnit union columns are walked by a
     // whole warp (its sub-warps split the columns).  The other vectors are
     // packed, in order, into batches of consecutive vectors walked by one
-    // sub-warp each; a batch holds at most 64 vectors and about `batch_cols`
-    // union columns, chosen so that there are ~64 batches per SM.  With R > 2
-    // a batch is one vector (vectors are long enough on their own).
+    // sub-warp each: a batch starts after a long unit, at every 64th short
+    // unit, and where the short units' running column count crosses a
+    // multiple of `batch_cols`, chosen so that there are ~64 batches per SM
+    // (the rule the GPU builder applies in parallel, panel_gpu_build.cu).
+    // With R > 2 a batch is one vector (vectors are long enough on their own).
     constexpr int kLongUnit = 128, kMaxBatchVecs = 64;
     std::vector<int> long_idx;
     std::vector<int4> batches;
@@ -292,6 +338,9 @@ vcsr_status vcsr_plan_create(const vcsr_csr *csr, int csr_where,
         if (cur.x >= 0) batches.push_back(cur);
         cur.x = -1;
       };
+      // short units so far; the exclusive column prefix at this short unit
+      // and at the previous one
+      int64_t k = 0, C = 0, prevC = 0;
       for (size_t u = 0; u < ph.units.size(); ++u) {
         const auto &un = ph.units[u];
         const int len = un.end - un.begin;
@@ -300,12 +349,15 @@ vcsr_status vcsr_plan_create(const vcsr_csr *csr, int csr_where,
           close();
           continue;
         }
-        if (cur.x >= 0 && (ph.R > 2 || cur.w - cur.z + len > batch_cols ||
-                           cur.y - cur.x >= kMaxBatchVecs))
+        if (cur.x >= 0 && (ph.R > 2 || k % kMaxBatchVecs == 0 ||
+                           C / batch_cols != prevC / batch_cols))
           close();
         if (cur.x < 0) cur = make_int4(un.vec, un.vec, un.begin, un.begin);
         cur.y = un.vec + 1;
         cur.w = un.end;
+        prevC = C;
+        C += len;
+        ++k;
       }
       close();
     }

@@ -150,7 +150,7 @@ vcsr_status vcsr_plan_save(const vcsr_plan *p, const char *path) {
           (int64_t)p->counter_stride, (int64_t)p->n_panel_rb, (int64_t)p->n_panel_blocks,
           p->panel_nnz, (int64_t)p->rpanels.size(), (int64_t)q.segw, (int64_t)q.bundle,
           (int64_t)q.tileK, (int64_t)q.max_O, (int64_t)q.vec_rows, (int64_t)q.chunk,
-          (int64_t)q.flags, (int64_t)q.panel_min_nnz, (int64_t)(p->has_ref ? 1 : 0),
+          (int64_t)(q.flags & ~VCSR_PLAN_HOST_BUILD), (int64_t)q.panel_min_nnz, (int64_t)(p->has_ref ? 1 : 0),
           (int64_t)g.M, (int64_t)g.N, (int64_t)g.segw, (int64_t)g.bundle, (int64_t)g.num_groups,
           (int64_t)g.num_segments, g.num_slots, (int64_t)q.target_O})
       w.i64(v);

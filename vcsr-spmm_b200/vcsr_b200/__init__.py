@@ -37,6 +37,7 @@ STATUS = {0: "ok", 1: "invalid", 2: "cuda", 3: "alloc", 4: "io",
 HOST, DEVICE = 0, 1
 PLAN_REFERENCE_FORMAT = 1
 PLAN_TF32_PANELS = 2
+PLAN_HOST_BUILD = 4
 MTX_BANNER = 1
 
 
@@ -464,7 +465,7 @@ class Plan:
 
     def __init__(self, csr, segw=4, bundle=32, tileK=0, max_O=512, vec_rows=0,
                  chunk=0, reference_format=False, tf32_panels=False, panel_min_nnz=0,
-                 target_O=0,
+                 target_O=0, host_build=False,
                  stream=None):
         L = lib()
         p = _PlanParams()
@@ -472,7 +473,8 @@ class Plan:
         p.segw, p.bundle, p.tileK, p.max_O = segw, bundle, tileK, max_O
         p.vec_rows, p.chunk = vec_rows, chunk
         p.flags = ((PLAN_REFERENCE_FORMAT if reference_format else 0)
-                   | (PLAN_TF32_PANELS if tf32_panels else 0))
+                   | (PLAN_TF32_PANELS if tf32_panels else 0)
+                   | (PLAN_HOST_BUILD if host_build else 0))
         p.panel_min_nnz = panel_min_nnz
         p.target_O = target_O
         where = DEVICE if isinstance(csr, DeviceCSR) else HOST

@@ -140,6 +140,14 @@ def _broadcast_and_multiply(dist, plan, dB, dC, src, chunks, stream):
     return early
 
 
+def sum_over_ranks(dist, value: int, device=None) -> int:
+    """An integer summed over every rank (e.g. the global row count)."""
+    import torch
+    t = torch.tensor([int(value)], dtype=torch.int64, device=device)
+    _collective("sum over ranks", lambda: dist.all_reduce(t, op=dist.ReduceOp.SUM))
+    return int(t.item())
+
+
 def max_over_ranks(dist, value: float, device=None) -> float:
     """The slowest rank's time."""
     import torch
