@@ -23,7 +23,7 @@
 extern "C" {
 #endif
 
-#define VCSR_ABI_VERSION 2
+#define VCSR_ABI_VERSION 3
 
 typedef void *vcsr_stream_t; /* a cudaStream_t */
 
@@ -179,6 +179,19 @@ typedef struct vcsr_plan vcsr_plan;
  * kernels that build it by default.  The layout is the same, bit for bit;
  * the flag exists to check the GPU builder against the host one. */
 #define VCSR_PLAN_HOST_BUILD 4
+/* Run A's column runs on the tensor cores at FP32 accuracy: every 16 rows
+ * (a row block) the union of their columns is cut into runs of consecutive
+ * columns, each run's B rows come into shared memory by TMA (the
+ * reference's B-tile-per-segment idea, src/kernels.cu:37-103), and
+ * tcgen05.mma kind::tf32 multiplies them by the row block's dense values with
+ * every value split into a TF32 high part and a TF32 remainder (three MMAs
+ * per step): results within about 1e-6 relative L2 of the CSR sum, and any
+ * output left non-finite is recomputed as the CSR sum is.  Runs shorter
+ * than seg_min_run columns stay on the FP32 kernel.  Pays where rows come
+ * in runs of consecutive columns (banded FEM matrices, dense blocks).
+ * Needs O and ldb multiples of 4 and a 16-byte aligned B at call time;
+ * built on the GPU only; excludes VCSR_PLAN_TF32_PANELS. */
+#define VCSR_PLAN_TC_SEGMENTS 8
 
 typedef struct vcsr_plan_params {
   int segw;     /* column segment width (--segw) */
@@ -195,6 +208,10 @@ typedef struct vcsr_plan_params {
                    vec_rows = 0 and target_O > 128 an 8-row choice becomes 4
                    rows (wider O: an 8-row vector's sums take 64 registers per
                    lane; measured 13-16% faster on FEM at O >= 192) */
+  int seg_min_run; /* VCSR_PLAN_TC_SEGMENTS: shortest column run on the tensor
+                      cores (0 = choose: runs under 8 columns are padded to 8
+                      while their padded rows stay below M, else left to the
+                      FP32 kernel) */
 } vcsr_plan_params;
 
 typedef struct vcsr_plan_info {
@@ -211,7 +228,11 @@ typedef struct vcsr_plan_info {
   double build_ms;    /* wall time of vcsr_plan_create */
   int num_panel_blocks;     /* dense 16x16 blocks on the TF32 path */
   int num_panel_row_blocks; /* row blocks holding them */
-  int64_t panel_nnz;        /* entries of A inside those blocks */
+  int64_t panel_nnz;        /* entries of A on the tensor cores */
+  int num_seg_row_blocks;   /* VCSR_PLAN_TC_SEGMENTS: row blocks with runs */
+  int num_seg_pieces;       /* pieces of at most 32 columns */
+  int64_t seg_rows;         /* B rows the pieces read (padding included) */
+  int seg_only;             /* 1: no residual; the segment kernel writes C alone */
 } vcsr_plan_info;
 
 void vcsr_plan_params_default(vcsr_plan_params *p);

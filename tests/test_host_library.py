@@ -29,7 +29,7 @@ def test_library_loads_and_exports_every_header_symbol():
     for name in declared:
         assert hasattr(L, name), name          # exported by the .so
         assert name in V.exported_names(), name  # and bound in Python
-    assert L.vcsr_abi_version() == 2
+    assert L.vcsr_abi_version() == 3
 
 
 def test_status_strings_and_last_error():

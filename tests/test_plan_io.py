@@ -39,12 +39,12 @@ def test_refuses_missing_and_foreign_files(tmp_path):
 
 def test_refuses_other_version_and_bad_header(tmp_path):
     p = os.path.join(tmp_path, "v.plan")
-    body = b"VCSRPLAN" + struct.pack("<qq", 99, 1) + bytes(8 * 35)
+    body = b"VCSRPLAN" + struct.pack("<qq", 99, 1) + bytes(8 * 41)
     with open(p, "wb") as f:
         f.write(body + struct.pack("<Q", fnv1a(body)))
     assert load_status(p) == 5
     abi = V.lib().vcsr_abi_version()
-    body = b"VCSRPLAN" + struct.pack("<qq", 3, abi) + struct.pack("<q", -5) + bytes(8 * 34)
+    body = b"VCSRPLAN" + struct.pack("<qq", 4, abi) + struct.pack("<q", -5) + bytes(8 * 40)
     with open(p, "wb") as f:
         f.write(body + struct.pack("<Q", fnv1a(body)))
     assert load_status(p) == 4  # negative M

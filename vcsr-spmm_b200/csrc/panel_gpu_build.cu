@@ -24,6 +24,7 @@
 #include "common.h"
 #include "device_prims.cuh"
 #include "panel_gpu.h"
+#include "seg_tc.h"
 
 namespace vcsr {
 namespace {
@@ -553,6 +554,106 @@ __global__ void batch_v0_kernel(const int *__restrict__ batches, int n, int *out
   GRID_STRIDE(i, n) out[i] = batches[4 * i];
 }
 
+// ------------------------------------------------- tensor-core segments
+// The 16-row union of vector v (R = 16 panels: ucol ascending, a duplicate
+// entry repeating its column) cut into runs of consecutive columns.  Pass 0
+// counts the runs shorter than 8 columns (*short_runs).  Pass 1 counts, per
+// vector, the runs of at least min_run columns, their pieces (at most
+// kSegPieceRows rows, a multiple of 8) and the pieces' rows.  Pass 2 writes
+// the runs {c0, length}, the pieces {c0, L, koff} and the dense tiles (values
+// of a column added in union order, which is CSR order for duplicates).
+__global__ void seg_runs_kernel(const int *__restrict__ vec_ptr, const int *__restrict__ ucol,
+                                const float *__restrict__ uval,
+                                const unsigned *__restrict__ umask, int V, int min_run,
+                                int pass, int *short_runs, int *nruns, int *npieces, int *nrows,
+                                const int *__restrict__ run_off,
+                                const int *__restrict__ piece_off,
+                                const int *__restrict__ row_off, int2 *runs, int4 *pieces,
+                                float *a) {
+  GRID_STRIDE(v, V) {
+    const int b = vec_ptr[v], e = vec_ptr[v + 1];
+    int nr = 0, np = 0, nk = 0, ns = 0;
+    int j = b;
+    while (j < e) {
+      // the run starting at union entry j: columns c0 .. c1-1, entries j .. j1-1
+      const int c0 = ucol[j];
+      int c1 = c0 + 1, j1 = j + 1;
+      while (j1 < e && (ucol[j1] == c1 - 1 || ucol[j1] == c1)) {
+        if (ucol[j1] == c1) ++c1;
+        ++j1;
+      }
+      const int len = c1 - c0;
+      if (len < 8) ++ns;
+      if (len >= min_run) {
+        const int pieces_here = (len + kSegPieceRows - 1) / kSegPieceRows;
+        if (pass == 2) {
+          const int kbase = row_off[v] + nk;
+          runs[run_off[v] + nr] = make_int2(c0, len);
+          for (int q = 0; q < pieces_here; ++q) {
+            const int rest = len - q * kSegPieceRows;
+            const int L = min(kSegPieceRows, (rest + 7) & ~7);
+            pieces[piece_off[v] + np + q] = make_int4(c0 + q * kSegPieceRows, L,
+                                                      kbase + q * kSegPieceRows, 0);
+          }
+          for (int jj = j; jj < j1; ++jj) {
+            const int k = ucol[jj] - c0, q = k / kSegPieceRows, kk = k % kSegPieceRows;
+            float *tile = a + (size_t)(kbase + q * kSegPieceRows) * 16;
+            const unsigned m = umask[jj];
+            for (int n = 0; n < 16; ++n)
+              if ((m >> n) & 1u)
+                tile[(kk / 4) * 64 + (n / 8) * 32 + (n % 8) * 4 + (kk % 4)] +=
+                    uval[(size_t)jj * 16 + n];
+          }
+        }
+        for (int q = 0; q < pieces_here; ++q) {
+          const int rest = len - q * kSegPieceRows;
+          nk += min(kSegPieceRows, (rest + 7) & ~7);
+        }
+        np += pieces_here;
+        ++nr;
+      }
+      j = j1;
+    }
+    if (pass == 0 && ns) atomicAdd(short_runs, ns);
+    if (pass == 1) {
+      nruns[v] = nr;
+      npieces[v] = np;
+      nrows[v] = nk;
+    }
+  }
+}
+
+// Entries outside every tensor-core run of their row block: the residual.
+__global__ void seg_residual_flags_kernel(const int *__restrict__ col,
+                                          const int *__restrict__ row_of, int nnz,
+                                          const int *__restrict__ run_off,
+                                          const int2 *__restrict__ runs, int *resid) {
+  GRID_STRIDE(p, nnz) {
+    const int v = row_of[p] >> 4, c = col[p];
+    int lo = run_off[v], hi = run_off[v + 1];
+    while (lo < hi) {  // first run starting after c
+      const int m = lo + ((hi - lo) >> 1);
+      if (runs[m].x <= c) lo = m + 1; else hi = m;
+    }
+    const bool in = lo > run_off[v] && c < runs[lo - 1].x + runs[lo - 1].y;
+    resid[p] = in ? 0 : 1;
+  }
+}
+
+// Row blocks holding pieces, compacted in order.
+__global__ void seg_row_blocks_kernel(const int *__restrict__ npieces,
+                                      const int *__restrict__ piece_off,
+                                      const int *__restrict__ rbi, int V, int n_pieces,
+                                      int *rb_row, int *pp) {
+  GRID_STRIDE(v, V) {
+    if (npieces[v] > 0) {
+      rb_row[rbi[v]] = (int)(16 * v);
+      pp[rbi[v]] = piece_off[v];
+    }
+    if (v == V - 1) pp[rbi[v] + (npieces[v] > 0 ? 1 : 0)] = n_pieces;
+  }
+}
+
 // The largest R <= 8 whose sampled vectors are at least 60% dense (the host
 // builder's choose_vec_rows, panel_build.cpp, on the same samples).
 vcsr_status choose_vec_rows_device(const vcsr_csr &w, int sms, Scratch &sc, int *R_out) {
@@ -661,6 +762,152 @@ vcsr_status build_plan_layout_device(vcsr_plan *p, const vcsr_csr &d, int sms,
     }
     p->n_panel_rb = n_rb;
     p->n_panel_blocks = n_blk;
+    p->panel_nnz = (int64_t)nnz - n_res;
+    work.nnz = n_res;
+    work.row_ptr = r_rp;
+    work.col = r_col;
+    work.val = r_val;
+  }
+
+  // ---- tensor-core segments: runs of consecutive columns of each 16-row
+  // block (spmm_seg_tc.cu); entries of shorter runs form the residual
+  if ((params.flags & VCSR_PLAN_TC_SEGMENTS) && M > 0) {
+    if (params.flags & VCSR_PLAN_TF32_PANELS)
+      return fail(VCSR_ERR_INVALID, "VCSR_PLAN_TC_SEGMENTS and VCSR_PLAN_TF32_PANELS exclude "
+                                    "each other");
+    if (params.seg_min_run < 0) return fail(VCSR_ERR_INVALID, "seg_min_run must be >= 0");
+    const int nnz = d.nnz, V16 = (int)ceil_div(M, 16);
+    int *row_of = nullptr, *flag = nullptr, *F = nullptr, *vp16 = nullptr, *uc16 = nullptr;
+    float *uv16 = nullptr;
+    unsigned *um16 = nullptr;
+    int *st_tot = nullptr;
+    VCSR_TRY(sc.get(&st_tot, 8));
+    VCSR_CUDA(cudaMemsetAsync(st_tot, 0, 8 * sizeof(int), st));
+    VCSR_TRY(sc.get(&row_of, nnz));
+    VCSR_TRY(sc.get(&flag, nnz));
+    VCSR_TRY(sc.get(&F, (int64_t)nnz + 1));
+    VCSR_TRY(sc.get(&vp16, (int64_t)V16 + 1));
+    row_of_kernel<<<grid_for((int64_t)M * 32), kThreads, 0, st>>>(d.row_ptr, M, row_of);
+    first_flag_kernel<<<grid_for(nnz), kThreads, 0, st>>>(d.row_ptr, d.col, row_of, nnz, 16,
+                                                           flag);
+    VCSR_CUDA(cudaGetLastError());
+    VCSR_TRY(scan_exclusive<int>(flag, F, nnz, F + nnz, sc));
+    int U16 = 0;
+    VCSR_TRY(read1(&U16, F + nnz, st));
+    VCSR_TRY(sc.get(&uc16, U16));
+    VCSR_TRY(sc.get(&uv16, (int64_t)U16 * 16));
+    VCSR_TRY(sc.get(&um16, U16));
+    VCSR_CUDA(cudaMemsetAsync(uv16, 0, sizeof(float) * 16 * (size_t)(U16 > 0 ? U16 : 1), st));
+    VCSR_CUDA(cudaMemsetAsync(um16, 0, sizeof(unsigned) * (size_t)(U16 > 0 ? U16 : 1), st));
+    vec_ptr_kernel<<<grid_for((int64_t)V16 + 1), kThreads, 0, st>>>(d.row_ptr, F, M, 16, V16,
+                                                                     vp16);
+    place_kernel<<<grid_for(nnz), kThreads, 0, st>>>(d.row_ptr, d.col, d.val, row_of, F, M, nnz,
+                                                      16, uc16, uv16, um16);
+    VCSR_CUDA(cudaGetLastError());
+    // Runs shorter than 8 columns: padded to 8 rows on the tensor cores while
+    // their padded rows stay below M (a residual pass costs C's write and a
+    // read-modify-write of C), else left to the FP32 kernel.
+    int min_run = params.seg_min_run;
+    if (min_run == 0) {
+      seg_runs_kernel<<<grid_for(V16), kThreads, 0, st>>>(
+          vp16, uc16, uv16, um16, V16, 1, 0, st_tot, nullptr, nullptr, nullptr, nullptr, nullptr,
+          nullptr, nullptr, nullptr, nullptr);
+      VCSR_CUDA(cudaGetLastError());
+      int short_runs = 0;
+      VCSR_TRY(read1(&short_runs, st_tot, st));
+      min_run = (int64_t)short_runs * 8 <= M ? 1 : 8;
+    }
+    int *nruns = nullptr, *npieces = nullptr, *nrows = nullptr, *run_off = nullptr,
+        *piece_off = nullptr, *row_off = nullptr, *pflag = nullptr, *rbi = nullptr;
+    VCSR_TRY(sc.get(&nruns, V16));
+    VCSR_TRY(sc.get(&npieces, V16));
+    VCSR_TRY(sc.get(&nrows, V16));
+    VCSR_TRY(sc.get(&run_off, (int64_t)V16 + 1));
+    VCSR_TRY(sc.get(&piece_off, (int64_t)V16 + 1));
+    VCSR_TRY(sc.get(&row_off, (int64_t)V16 + 1));
+    seg_runs_kernel<<<grid_for(V16), kThreads, 0, st>>>(
+        vp16, uc16, uv16, um16, V16, min_run, 1, nullptr, nruns, npieces, nrows, nullptr,
+        nullptr, nullptr, nullptr, nullptr, nullptr);
+    VCSR_CUDA(cudaGetLastError());
+    VCSR_TRY(scan_exclusive<int>(nruns, run_off, V16, run_off + V16, sc));
+    VCSR_TRY(scan_exclusive<int>(npieces, piece_off, V16, piece_off + V16, sc));
+    VCSR_TRY(scan_exclusive<int>(nrows, row_off, V16, row_off + V16, sc));
+    int h3[3];
+    VCSR_TRY(read1(&h3[0], run_off + V16, st));
+    VCSR_TRY(read1(&h3[1], piece_off + V16, st));
+    VCSR_TRY(read1(&h3[2], row_off + V16, st));
+    const int n_runs = h3[0], n_pieces = h3[1], seg_rows = h3[2];
+    int2 *runs = nullptr;
+    VCSR_TRY(sc.get(&runs, n_runs));
+    VCSR_TRY(dmalloc(&p->d_seg_pieces, n_pieces));
+    VCSR_TRY(dmalloc(&p->d_seg_a, (int64_t)seg_rows * 16));
+    VCSR_CUDA(cudaMemsetAsync(p->d_seg_a, 0, sizeof(float) * 16 * (size_t)(seg_rows > 0 ? seg_rows : 1),
+                              st));
+    seg_runs_kernel<<<grid_for(V16), kThreads, 0, st>>>(
+        vp16, uc16, uv16, um16, V16, min_run, 2, nullptr, nullptr, nullptr, nullptr, run_off,
+        piece_off, row_off, runs, p->d_seg_pieces, p->d_seg_a);
+    VCSR_CUDA(cudaGetLastError());
+    sc.release(uc16);
+    sc.release(uv16);
+    sc.release(um16);
+    // row blocks with pieces
+    VCSR_TRY(sc.get(&pflag, V16));
+    VCSR_TRY(sc.get(&rbi, (int64_t)V16 + 1));
+    positive_flags_kernel<<<grid_for(V16), kThreads, 0, st>>>(npieces, V16, pflag);
+    VCSR_CUDA(cudaGetLastError());
+    VCSR_TRY(scan_exclusive<int>(pflag, rbi, V16, rbi + V16, sc));
+    int n_seg_rb = 0;
+    VCSR_TRY(read1(&n_seg_rb, rbi + V16, st));
+    VCSR_TRY(dmalloc(&p->d_seg_rb_row, n_seg_rb));
+    VCSR_TRY(dmalloc(&p->d_seg_pp, (int64_t)n_seg_rb + 1));
+    seg_row_blocks_kernel<<<grid_for(V16), kThreads, 0, st>>>(npieces, piece_off, rbi, V16,
+                                                               n_pieces, p->d_seg_rb_row,
+                                                               p->d_seg_pp);
+    VCSR_CUDA(cudaGetLastError());
+    // the residual: entries outside every run of their row block
+    int *resid = flag;  // reused
+    seg_residual_flags_kernel<<<grid_for(nnz), kThreads, 0, st>>>(d.col, row_of, nnz, run_off,
+                                                                   runs, resid);
+    VCSR_CUDA(cudaGetLastError());
+    VCSR_TRY(scan_exclusive<int>(resid, F, nnz, F + nnz, sc));
+    int n_res = 0;
+    VCSR_TRY(read1(&n_res, F + nnz, st));
+    int *r_rp = nullptr, *r_col = nullptr;
+    float *r_val = nullptr;
+    VCSR_TRY(sc.get(&r_rp, (int64_t)M + 1));
+    VCSR_TRY(sc.get(&r_col, n_res));
+    VCSR_TRY(sc.get(&r_val, n_res));
+    residual_kernel<<<grid_for(std::max<int64_t>(nnz, (int64_t)M + 1)), kThreads, 0, st>>>(
+        d.row_ptr, d.col, d.val, resid, F, M, nnz, r_rp, r_col, r_val);
+    VCSR_CUDA(cudaGetLastError());
+    // the whole CSR, for the exact recomputation of non-finite outputs
+    VCSR_TRY(dmalloc(&p->d_seg_rp, (int64_t)M + 1));
+    VCSR_TRY(dmalloc(&p->d_seg_col, nnz));
+    VCSR_TRY(dmalloc(&p->d_seg_val, nnz));
+    VCSR_CUDA(cudaMemcpyAsync(p->d_seg_rp, d.row_ptr, sizeof(int) * ((size_t)M + 1),
+                              cudaMemcpyDeviceToDevice, st));
+    if (nnz) {
+      VCSR_CUDA(cudaMemcpyAsync(p->d_seg_col, d.col, sizeof(int) * (size_t)nnz,
+                                cudaMemcpyDeviceToDevice, st));
+      VCSR_CUDA(cudaMemcpyAsync(p->d_seg_val, d.val, sizeof(float) * (size_t)nnz,
+                                cudaMemcpyDeviceToDevice, st));
+    }
+    if (!p->d_err && n_seg_rb > 0) {
+      VCSR_TRY(dmalloc(&p->d_err, 1));
+      VCSR_CUDA(cudaMemsetAsync(p->d_err, 0, sizeof(int), st));
+    }
+    p->n_seg_rb = n_seg_rb;
+    p->n_seg_pieces = n_pieces;
+    p->seg_rows = seg_rows;
+    p->seg_min_run = min_run;
+    p->seg_only = n_res == 0 && n_seg_rb == V16;
+    acct(p, 4, n_seg_rb);
+    acct(p, 4, (int64_t)n_seg_rb + 1);
+    acct(p, 16, n_pieces);
+    acct(p, 4, (int64_t)seg_rows * 16);
+    acct(p, 4, (int64_t)M + 1);
+    acct(p, 4, nnz);
+    acct(p, 4, nnz);
     p->panel_nnz = (int64_t)nnz - n_res;
     work.nnz = n_res;
     work.row_ptr = r_rp;
@@ -817,7 +1064,7 @@ vcsr_status build_plan_layout_device(vcsr_plan *p, const vcsr_csr &d, int sms,
   // ---- row panels of the host entry point's row pipeline (plan.cu): cut at
   // vectors where a batch or a long unit starts, near 1/32, 1/6, ..., 5/6,
   // 31/32 of the entries
-  if (p->n_panel_rb == 0 && M >= 8192 && nnz >= (1 << 20)) {
+  if (p->n_panel_rb == 0 && p->n_seg_rb == 0 && M >= 8192 && nnz >= (1 << 20)) {
     constexpr int kRowPanels = 8;
     constexpr double kCut[kRowPanels - 1] = {1.0 / 32, 1.0 / 6, 2.0 / 6, 3.0 / 6,
                                              4.0 / 6,  5.0 / 6, 31.0 / 32};

@@ -18,6 +18,7 @@
 #include "plan_impl.h"
 #include "panel_tc.h"
 #include "spmm_kernels.h"
+#include "seg_tc.h"
 #include "spmm_tc.h"
 
 using vcsr::fail;
@@ -33,6 +34,8 @@ void plan_release(vcsr_plan *p) {
   if (p->has_ref) vcsr_vcsr_free(&p->ref, VCSR_DEVICE);
   cudaFree(p->d_rb_row); cudaFree(p->d_rb_ptr); cudaFree(p->d_blk_col);
   cudaFree(p->d_blk_val); cudaFree(p->d_err);
+  cudaFree(p->d_seg_rb_row); cudaFree(p->d_seg_pp); cudaFree(p->d_seg_pieces);
+  cudaFree(p->d_seg_a); cudaFree(p->d_seg_rp); cudaFree(p->d_seg_col); cudaFree(p->d_seg_val);
   if (p->side) cudaStreamDestroy(p->side);
   if (p->down) cudaStreamDestroy(p->down);
   if (p->comp) cudaStreamDestroy(p->comp);
@@ -209,6 +212,7 @@ void vcsr_plan_params_default(vcsr_plan_params *p) {
   p->flags = 0;
   p->panel_min_nnz = 0;
   p->target_O = 0;
+  p->seg_min_run = 0;
 }
 
 vcsr_status vcsr_plan_create(const vcsr_csr *csr, int csr_where,
@@ -249,6 +253,10 @@ vcsr_status vcsr_plan_create(const vcsr_csr *csr, int csr_where,
       return VCSR_OK;
     }
 
+    if (params->flags & VCSR_PLAN_TC_SEGMENTS) {
+      delete p;
+      return fail(VCSR_ERR_UNSUPPORTED, "tensor-core segments are built on the GPU only");
+    }
     vcsr_csr h{};
     bool owned = false;
     vcsr_csr empty_rp{};
@@ -491,6 +499,10 @@ vcsr_status vcsr_plan_get_info(const vcsr_plan *p, vcsr_plan_info *info) {
   info->num_panel_blocks = p->n_panel_blocks;
   info->num_panel_row_blocks = p->n_panel_rb;
   info->panel_nnz = p->panel_nnz;
+  info->num_seg_row_blocks = p->n_seg_rb;
+  info->num_seg_pieces = p->n_seg_pieces;
+  info->seg_rows = p->seg_rows;
+  info->seg_only = p->seg_only ? 1 : 0;
   return VCSR_OK;
 }
 
@@ -524,6 +536,26 @@ vcsr_status vcsr_spmm(const vcsr_plan *p, const float *dB, int ldb, float *dC,
                 "O=%d exceeds the plan's max_O=%d (split rows need scratch)", O,
                 p->pstride);
   int n1 = 0, n2 = 0;
+  if (p->n_seg_rb > 0) {  // tensor-core segments; the residual (if any) first
+    if (!p->seg_only)
+      VCSR_TRY(vcsr::launch_panel_spmm(view(p), false, dB, ldb, dC, ldc, O,
+                                       (cudaStream_t)stream, &n1, p->side, p->fork, p->join));
+    vcsr::SegView sv;
+    sv.n_rb = p->n_seg_rb;
+    sv.rb_row = p->d_seg_rb_row;
+    sv.pp = p->d_seg_pp;
+    sv.pieces = p->d_seg_pieces;
+    sv.a = p->d_seg_a;
+    sv.rp = p->d_seg_rp;
+    sv.col = p->d_seg_col;
+    sv.val = p->d_seg_val;
+    sv.M = p->M;
+    sv.accumulate = p->seg_only ? 0 : 1;
+    sv.err = p->d_err;
+    VCSR_TRY(vcsr::launch_seg_tc(sv, dB, p->N, ldb, dC, ldc, O, (cudaStream_t)stream, &n2));
+    if (launches) *launches = n1 + n2;
+    return VCSR_OK;
+  }
   VCSR_TRY(vcsr::launch_panel_spmm(view(p), false, dB, ldb, dC, ldc, O, (cudaStream_t)stream,
                                    &n1, p->side, p->fork, p->join));
   if (p->n_panel_rb > 0) {  // C += dense panels * B on the tensor cores
@@ -596,8 +628,9 @@ vcsr_status spmm_16bit(const vcsr_plan *p, const void *dB, int ldb, float *dC, i
     return fail(VCSR_ERR_INVALID, "need 0 <= O <= ldb, ldc (O=%d ldb=%d ldc=%d)", O, ldb, ldc);
   if (O == 0 || p->M == 0) return VCSR_OK;
   if (!dC || (!dB && p->N > 0)) return fail(VCSR_ERR_INVALID, "null B or C");
-  if (p->n_panel_rb > 0)
-    return fail(VCSR_ERR_UNSUPPORTED, "a plan with TF32 panels reads B in FP32");
+  if (p->n_panel_rb > 0 || p->n_seg_rb > 0)
+    return fail(VCSR_ERR_UNSUPPORTED,
+                "a plan with tensor-core panels or segments reads B in FP32");
   if ((uintptr_t)dB % 2) return fail(VCSR_ERR_INVALID, "%s B must be 2-byte aligned", name);
   if (p->n_split_units > 0 && O > p->pstride)
     return fail(VCSR_ERR_INVALID,

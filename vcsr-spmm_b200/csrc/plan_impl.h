@@ -39,6 +39,14 @@ struct vcsr_plan {
   int *d_rb_row = nullptr, *d_rb_ptr = nullptr, *d_blk_col = nullptr, *d_err = nullptr;
   float *d_blk_val = nullptr;
   int n_panel_rb = 0, n_panel_blocks = 0;
+  // tensor-core segments (VCSR_PLAN_TC_SEGMENTS, seg_tc.h): row blocks with
+  // pieces, the pieces, their dense tiles, and the whole CSR for recomputing
+  // non-finite outputs; seg_only: no residual, the segment kernel writes C
+  int *d_seg_rb_row = nullptr, *d_seg_pp = nullptr, *d_seg_rp = nullptr, *d_seg_col = nullptr;
+  int4 *d_seg_pieces = nullptr;
+  float *d_seg_a = nullptr, *d_seg_val = nullptr;
+  int n_seg_rb = 0, n_seg_pieces = 0, seg_rows = 0, seg_min_run = 0;
+  bool seg_only = false;
   // test hook (vcsr_plan_test_withhold_signal): the next TF32 panel launch
   // withholds one barrier signal; one-shot
   mutable std::atomic<int> tc_inject{0};

@@ -24,7 +24,7 @@ using vcsr::fail;
 namespace {
 
 constexpr char kMagic[8] = {'V', 'C', 'S', 'R', 'P', 'L', 'A', 'N'};
-constexpr int64_t kVersion = 3;
+constexpr int64_t kVersion = 4;
 
 uint64_t fnv1a(const unsigned char *p, size_t n) {
   uint64_t h = 1469598103934665603ull;
@@ -96,6 +96,9 @@ vcsr_status upload_n(T **dst, const std::vector<T> &src, cudaStream_t st) {
 struct HostPlan {
   std::vector<int> ucol, long_idx, vec_ptr, rb_row, rb_ptr, blk_col, rpan;
   std::vector<unsigned> umask;
+  std::vector<int> seg_rb, seg_pp, seg_rp, seg_col;
+  std::vector<int4> seg_pieces;
+  std::vector<float> seg_a, seg_val;
   std::vector<float> uval, blk_val;
   std::vector<int4> units, batches;
   std::vector<int2> parts, svecs;
@@ -127,7 +130,16 @@ vcsr_status vcsr_plan_save(const vcsr_plan *p, const char *path) {
       VCSR_TRY(download(h.blk_col, p->d_blk_col, p->n_panel_blocks));
       VCSR_TRY(download(h.blk_val, p->d_blk_val, (int64_t)p->n_panel_blocks * 256));
     }
-    for (const auto &r : p->rpanels)
+    if (p->n_seg_rb > 0) {
+    VCSR_TRY(download(h.seg_rb, p->d_seg_rb_row, p->n_seg_rb));
+    VCSR_TRY(download(h.seg_pp, p->d_seg_pp, (int64_t)p->n_seg_rb + 1));
+    VCSR_TRY(download(h.seg_pieces, p->d_seg_pieces, p->n_seg_pieces));
+    VCSR_TRY(download(h.seg_a, p->d_seg_a, (int64_t)p->seg_rows * 16));
+    VCSR_TRY(download(h.seg_rp, p->d_seg_rp, (int64_t)p->M + 1));
+    VCSR_TRY(download(h.seg_col, p->d_seg_col, p->nnz));
+    VCSR_TRY(download(h.seg_val, p->d_seg_val, p->nnz));
+  }
+  for (const auto &r : p->rpanels)
       for (int v : {r.row0, r.row1, r.b0, r.b1, r.l0, r.l1, r.col_max}) h.rpan.push_back(v);
     const vcsr_vcsr &g = p->ref;
     if (p->has_ref) {
@@ -152,13 +164,17 @@ vcsr_status vcsr_plan_save(const vcsr_plan *p, const char *path) {
           (int64_t)q.tileK, (int64_t)q.max_O, (int64_t)q.vec_rows, (int64_t)q.chunk,
           (int64_t)(q.flags & ~VCSR_PLAN_HOST_BUILD), (int64_t)q.panel_min_nnz, (int64_t)(p->has_ref ? 1 : 0),
           (int64_t)g.M, (int64_t)g.N, (int64_t)g.segw, (int64_t)g.bundle, (int64_t)g.num_groups,
-          (int64_t)g.num_segments, g.num_slots, (int64_t)q.target_O})
+          (int64_t)g.num_segments, g.num_slots, (int64_t)q.target_O, (int64_t)q.seg_min_run,
+        (int64_t)p->n_seg_rb, (int64_t)p->n_seg_pieces, (int64_t)p->seg_rows,
+        (int64_t)p->seg_min_run, (int64_t)(p->seg_only ? 1 : 0)})
       w.i64(v);
     w.arr(h.ucol); w.arr(h.uval); w.arr(h.umask); w.arr(h.units); w.arr(h.batches); w.arr(h.long_idx);
     w.arr(h.vec_ptr); w.arr(h.parts); w.arr(h.svecs); w.arr(h.rb_row); w.arr(h.rb_ptr);
     w.arr(h.blk_col); w.arr(h.blk_val); w.arr(h.rpan);
     w.arr(h.g_ptr); w.arr(h.g_depth); w.arr(h.g_seg); w.arr(h.g_rows); w.arr(h.g_lcol);
     w.arr(h.g_val); w.arr(h.g_sgs);
+  w.arr(h.seg_rb); w.arr(h.seg_pp); w.arr(h.seg_pieces); w.arr(h.seg_a); w.arr(h.seg_rp);
+  w.arr(h.seg_col); w.arr(h.seg_val);
     const uint64_t hash = fnv1a(w.buf.data(), w.buf.size());
     w.raw(&hash, 8);
     // write beside the target, then rename: a reader never sees half a file
@@ -201,7 +217,7 @@ vcsr_status vcsr_plan_load(const char *path, vcsr_plan **out, vcsr_stream_t stre
     if (!r.ok || version != kVersion || abi != VCSR_ABI_VERSION)
       return fail(VCSR_ERR_UNSUPPORTED, "plan file version %lld (ABI %lld); this library reads %lld (ABI %d)",
                   (long long)version, (long long)abi, (long long)kVersion, VCSR_ABI_VERSION);
-    int64_t hv[35];
+    int64_t hv[41];
     for (int64_t &v : hv) v = r.i64();
     if (!r.ok) return fail(VCSR_ERR_IO, "plan file %s is truncated", path);
     const int64_t M = hv[0], N = hv[1], nnz = hv[2], R = hv[3], nv = hv[4], nu = hv[5],
@@ -209,6 +225,7 @@ vcsr_status vcsr_plan_load(const char *path, vcsr_plan **out, vcsr_stream_t stre
                   n_l = hv[11], pstride = hv[12], cstride = hv[13], n_rb = hv[14],
                   n_blk = hv[15], panel_nnz = hv[16], n_rp = hv[17];
     const int64_t has_ref = hv[26];
+  const int64_t s_rb = hv[36], s_np = hv[37], s_rows = hv[38], s_min = hv[39], s_only = hv[40];
     const int64_t gM = hv[27], gN = hv[28], g_segw = hv[29], g_bundle = hv[30], g_G = hv[31],
                   g_S = hv[32], g_P = hv[33];
     const int64_t i32 = INT32_MAX;
@@ -219,7 +236,9 @@ vcsr_status vcsr_plan_load(const char *path, vcsr_plan **out, vcsr_stream_t stre
               n_l >= 0 && n_l <= n_units && pstride >= 1 && pstride <= i32 && cstride >= 1 &&
               cstride <= i32 && n_rb >= 0 && n_rb <= (M + 15) / 16 && n_blk >= n_rb &&
               n_blk <= i32 && panel_nnz >= 0 && n_rp >= 0 && n_rp <= 1024 && chunk >= 0 &&
-              (has_ref == 0 || has_ref == 1);
+              (has_ref == 0 || has_ref == 1) && s_rb >= 0 && s_rb <= (M + 15) / 16 &&
+            s_np >= s_rb && s_np <= i32 && s_rows >= 0 && s_rows * 16 <= i32 && s_min >= 0 &&
+            (s_only == 0 || s_only == 1) && !(s_rb > 0 && n_rb > 0);
     if (has_ref)
       ok = ok && gM == M && gN == N && g_segw > 0 && g_bundle > 0 && g_G >= 0 && g_G <= i32 &&
            g_S >= 0 && g_S <= i32 && g_P >= 0 && g_P <= i32;
@@ -246,6 +265,13 @@ vcsr_status vcsr_plan_load(const char *path, vcsr_plan **out, vcsr_stream_t stre
     h.g_lcol = r.arr<int>(has_ref ? g_P : 0);
     h.g_val = r.arr<float>(has_ref ? g_P : 0);
     h.g_sgs = r.arr<int>(has_ref ? g_S + 1 : 0);
+  h.seg_rb = r.arr<int>(s_rb);
+  h.seg_pp = r.arr<int>(s_rb ? s_rb + 1 : 0);
+  h.seg_pieces = r.arr<int4>(s_rb ? s_np : 0);
+  h.seg_a = r.arr<float>(s_rb ? s_rows * 16 : 0);
+  h.seg_rp = r.arr<int>(s_rb ? M + 1 : 0);
+  h.seg_col = r.arr<int>(s_rb ? nnz : 0);
+  h.seg_val = r.arr<float>(s_rb ? nnz : 0);
     if (!r.ok || r.p != r.end) return fail(VCSR_ERR_IO, "plan file %s has bad array sizes", path);
     // every index the kernels follow
     for (int c : h.ucol) ok = ok && c >= 0 && c < N;
@@ -282,7 +308,19 @@ vcsr_status vcsr_plan_load(const char *path, vcsr_plan **out, vcsr_stream_t stre
       for (int x : h.g_lcol) ok = ok && x >= -1 && x < g_segw;
       for (int x : h.g_sgs) ok = ok && x >= 0 && x <= g_G;
     }
-    if (!ok) return fail(VCSR_ERR_IO, "plan file %s has out-of-range indices", path);
+    if (s_rb) {
+    ok = ok && h.seg_pp[0] == 0 && h.seg_pp[(size_t)s_rb] == s_np;
+    for (int64_t k = 0; k < s_rb && ok; ++k)
+      ok = h.seg_rb[(size_t)k] >= 0 && h.seg_rb[(size_t)k] < M && h.seg_rb[(size_t)k] % 16 == 0 &&
+           h.seg_pp[(size_t)k] < h.seg_pp[(size_t)k + 1];
+    for (const int4 &q : h.seg_pieces)
+      ok = ok && q.x >= 0 && q.x < N && q.y >= 8 && q.y <= 32 && q.y % 8 == 0 && q.z >= 0 &&
+           q.z % 8 == 0 && (int64_t)q.z + q.y <= s_rows;
+    ok = ok && h.seg_rp[0] == 0 && h.seg_rp[(size_t)M] == nnz;
+    for (int64_t k = 0; k < M && ok; ++k) ok = h.seg_rp[(size_t)k] <= h.seg_rp[(size_t)k + 1];
+    for (int c : h.seg_col) ok = ok && c >= 0 && c < N;
+  }
+  if (!ok) return fail(VCSR_ERR_IO, "plan file %s has out-of-range indices", path);
 
     // the device side
     vcsr_plan *p = new (std::nothrow) vcsr_plan();
@@ -298,6 +336,12 @@ vcsr_status vcsr_plan_load(const char *path, vcsr_plan **out, vcsr_stream_t stre
     p->params.max_O = (int)hv[21]; p->params.vec_rows = (int)hv[22]; p->params.chunk = (int)hv[23];
     p->params.flags = (int)hv[24]; p->params.panel_min_nnz = (int)hv[25];
     p->params.target_O = (int)hv[34];
+  p->params.seg_min_run = (int)hv[35];
+  p->n_seg_rb = (int)s_rb;
+  p->n_seg_pieces = s_rb ? (int)s_np : 0;
+  p->seg_rows = s_rb ? (int)s_rows : 0;
+  p->seg_min_run = (int)s_min;
+  p->seg_only = s_only == 1;
     cudaGetDevice(&p->device);
     for (int64_t j = 0; j < n_rp; ++j) {
       const int *q = &h.rpan[(size_t)j * 7];
@@ -319,6 +363,14 @@ vcsr_status vcsr_plan_load(const char *path, vcsr_plan **out, vcsr_stream_t stre
                   (s = vcsr::upload(&p->d_blk_col, h.blk_col, st, &p->panel_bytes)) ||
                   (s = vcsr::upload(&p->d_blk_val, h.blk_val, st, &p->panel_bytes)) ||
                   (s = vcsr::upload(&p->d_err, zero1, st, &p->panel_bytes)))) ||
+      (s_rb && ((s = vcsr::upload(&p->d_seg_rb_row, h.seg_rb, st, &p->panel_bytes)) ||
+                (s = vcsr::upload(&p->d_seg_pp, h.seg_pp, st, &p->panel_bytes)) ||
+                (s = vcsr::upload(&p->d_seg_pieces, h.seg_pieces, st, &p->panel_bytes)) ||
+                (s = vcsr::upload(&p->d_seg_a, h.seg_a, st, &p->panel_bytes)) ||
+                (s = vcsr::upload(&p->d_seg_rp, h.seg_rp, st, &p->panel_bytes)) ||
+                (s = vcsr::upload(&p->d_seg_col, h.seg_col, st, &p->panel_bytes)) ||
+                (s = vcsr::upload(&p->d_seg_val, h.seg_val, st, &p->panel_bytes)) ||
+                (s = vcsr::upload(&p->d_err, zero1, st, nullptr)))) ||
         (s = vcsr::plan_finish(p, st))) {
       vcsr::plan_release(p);
       delete p;

@@ -2,6 +2,7 @@
 #pragma once
 #include <cstddef>
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include "common.h"
@@ -34,6 +35,15 @@ struct TcView {
 };
 
 size_t tc_smem_bytes();
+
+// cuTensorMapEncodeTiled, found once through the runtime's driver entry
+// point (the library does not link the driver library).
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                   CUtensorMapFloatOOBfill);
+vcsr_status tensor_map_encoder(EncodeTiledFn *out);
 
 // Text for a nonzero error word.
 void describe_tc_error(int word, char *buf, size_t n);

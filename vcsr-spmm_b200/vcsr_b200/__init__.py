@@ -38,6 +38,7 @@ HOST, DEVICE = 0, 1
 PLAN_REFERENCE_FORMAT = 1
 PLAN_TF32_PANELS = 2
 PLAN_HOST_BUILD = 4
+PLAN_TC_SEGMENTS = 8
 MTX_BANNER = 1
 
 
@@ -71,7 +72,8 @@ class _Vcsr(C.Structure):
 class _PlanParams(C.Structure):
     _fields_ = [("segw", C.c_int), ("bundle", C.c_int), ("tileK", C.c_int),
                 ("max_O", C.c_int), ("vec_rows", C.c_int), ("chunk", C.c_int),
-                ("flags", C.c_int), ("panel_min_nnz", C.c_int), ("target_O", C.c_int)]
+                ("flags", C.c_int), ("panel_min_nnz", C.c_int), ("target_O", C.c_int),
+                ("seg_min_run", C.c_int)]
 
 
 class _PlanInfo(C.Structure):
@@ -81,7 +83,9 @@ class _PlanInfo(C.Structure):
                 ("num_split_vectors", C.c_int), ("num_split_units", C.c_int),
                 ("num_long_units", C.c_int), ("panel_bytes", C.c_int64), ("has_reference_format", C.c_int),
                 ("build_ms", C.c_double), ("num_panel_blocks", C.c_int),
-                ("num_panel_row_blocks", C.c_int), ("panel_nnz", C.c_int64)]
+                ("num_panel_row_blocks", C.c_int), ("panel_nnz", C.c_int64),
+                ("num_seg_row_blocks", C.c_int), ("num_seg_pieces", C.c_int),
+                ("seg_rows", C.c_int64), ("seg_only", C.c_int)]
 
 
 _LIB = None
@@ -465,7 +469,7 @@ class Plan:
 
     def __init__(self, csr, segw=4, bundle=32, tileK=0, max_O=512, vec_rows=0,
                  chunk=0, reference_format=False, tf32_panels=False, panel_min_nnz=0,
-                 target_O=0, host_build=False,
+                 target_O=0, host_build=False, tc_segments=False, seg_min_run=0,
                  stream=None):
         L = lib()
         p = _PlanParams()
@@ -474,9 +478,11 @@ class Plan:
         p.vec_rows, p.chunk = vec_rows, chunk
         p.flags = ((PLAN_REFERENCE_FORMAT if reference_format else 0)
                    | (PLAN_TF32_PANELS if tf32_panels else 0)
-                   | (PLAN_HOST_BUILD if host_build else 0))
+                   | (PLAN_HOST_BUILD if host_build else 0)
+                   | (PLAN_TC_SEGMENTS if tc_segments else 0))
         p.panel_min_nnz = panel_min_nnz
         p.target_O = target_O
+        p.seg_min_run = seg_min_run
         where = DEVICE if isinstance(csr, DeviceCSR) else HOST
         s = csr._struct()
         h = C.c_void_p()

@@ -6,8 +6,9 @@ by a broadcast (NCCL over NVLink on GPUs; gloo in the CPU tests), C panels are
 disjoint so nothing is reduced, and a timing is the max over ranks.
 
 Two ways to own rows:
-  * "strong": one global matrix, cut into nnz-balanced panels
-    (vcsr_partition_rows, cuts aligned to `align` rows);
+  * "strong": one global matrix, cut into panels of balanced cost (nnz plus
+    a per-row weight, vcsr_partition_rows_weighted; cuts aligned to `align`
+    rows);
   * "weak": every rank owns a full panel of its own (seed + rank), so the
     global matrix has world * M rows and per-rank work is fixed.
 """
@@ -46,8 +47,17 @@ def _collective(what, fn):
         raise VcsrError(STATUS_NCCL, f"{what}: a peer rank failed, left or timed out: {e}") from e
 
 
+# Strong scaling cuts A into panels of equal nnz + ROW_WEIGHT * rows.  Each
+# row also costs its C row write (as many bytes as one entry's B row) and
+# its own set-up: measured on two B200s on R-MAT 2^22 at O = 256, panels of
+# equal nnz took 3.15 ms (0.59M rows) and 3.72 ms (3.6M rows), i.e. about
+# 0.093 ms per million entries and 0.19 ms per million rows: a row weighs
+# about two entries.
+ROW_WEIGHT = 2.0
+
+
 def rank_panel(config: str, size: int, seed: int, rank: int, world: int,
-               scaling: str, align: int = 16):
+               scaling: str, align: int = 16, row_weight: float = ROW_WEIGHT):
     """(panel CSR, first global row, global nnz) of this rank."""
     if scaling == "weak":
         csr = gen_csr(config, seed + rank, size)
@@ -55,7 +65,7 @@ def rank_panel(config: str, size: int, seed: int, rank: int, world: int,
     full = gen_csr(config, seed, size)
     if world == 1:
         return full, 0, full.nnz
-    cuts = partition_rows(full.row_ptr, world, align)
+    cuts = partition_rows(full.row_ptr, world, align, row_weight)
     panel = csr_row_panel(full, int(cuts[rank]), int(cuts[rank + 1]))
     return panel, int(cuts[rank]), full.nnz
 
