@@ -290,12 +290,25 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    import vcsr_b200 as V
     cfg, size, O, scaling, label = WORKLOADS[args.workload]
     if args.size is not None:
         size, label = args.size, f"{label}@size{args.size}"
-    csr = V.gen_csr(cfg, args.seed, size)
-    B = V.gen_dense_host(csr.N, O, args.seed + 1000, 0.0 if cfg == "rmat" else -1.0, 1.0)
+    lo = 0.0 if cfg == "rmat" else -1.0
+    if cfg == "rmat":
+        # the same seeded inputs, restated in the oracle: this arm loads
+        # nothing of the engine
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import types
+        import oracle
+        M, rp, col, val = oracle.gen_rmat(size, args.seed)
+        csr = types.SimpleNamespace(M=M, N=M, nnz=len(col), row_ptr=rp, col=col, val=val)
+        B = oracle.gen_dense(M, O, args.seed + 1000, lo, 1.0)
+        inputs = "oracle restatement of the engine's seeded generators (bit-identical)"
+    else:
+        import vcsr_b200 as V
+        csr = V.gen_csr(cfg, args.seed, size)
+        B = V.gen_dense_host(csr.N, O, args.seed + 1000, lo, 1.0)
+        inputs = "the engine library's seeded generators"
     per_step = max(1.0, args.cpu_seconds / max(1, args.steps))
     for _ in range(args.warmup):
         cpu_reference(csr, B, 0.0, min_reps=1)
@@ -315,6 +328,7 @@ def run_reference(args):
             "config": workload_config(label, csr.M, csr.N, csr.nnz, O, world),
             "algorithm": "reference CSR SpMM (src/kernels.cu:15-33) on host cores, "
                          "OpenMP over rows",
+            "inputs": inputs,
             "cpu_baseline": dict(info, value=round(v, 3), cpu_model=cpu_model()),
             "e2e": {"value": round(v, 3), "unit": "GFLOP/s",
                     "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}

@@ -460,3 +460,127 @@ void oracle_vcsr_spmm(const oracle_vcsr *v, const float *B, int O, float *C) {
       }
   }
 }
+
+/* ------------------------------------------------------------ inputs
+ * The benchmark's seeded inputs restated for the CPU reference arm, so that
+ * arm builds them without loading the engine library: the R-MAT matrix and
+ * the dense fill of the engine's generators (vcsr-spmm_b200/csrc/gen.cpp
+ * gen_rmat, csrc/memory.cu vcsr_gen_dense).  Random numbers: SplitMix64's
+ * output function (Steele, Lea & Flood, OOPSLA 2014) on key + index, with
+ * key = mix(seed * 0xD1B54A32D192ED03 ^ mix(stream)).  Pinned bit for bit
+ * against the library by tests/test_oracle_golden.py. */
+static inline uint64_t og_mix(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+static inline uint64_t og_key(uint64_t seed, uint64_t stream) {
+  return og_mix(seed * 0xD1B54A32D192ED03ull ^ og_mix(stream));
+}
+static inline float og_u01f(uint64_t x) {
+  return (float)(uint32_t)(x >> 40) * (1.0f / 16777216.0f);
+}
+
+/* rows x cols row-major: element i = lo + (hi - lo) * u01(mix(key + i)). */
+void oracle_gen_dense(float *out, int64_t rows, int64_t cols, uint64_t seed, float lo,
+                      float hi) {
+  const uint64_t key = og_key(seed, 0xB0B0ull);
+  const int64_t n = rows * cols;
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < n; ++i) out[i] = lo + (hi - lo) * og_u01f(og_mix(key + (uint64_t)i));
+}
+
+static int og_cmp_int(const void *a, const void *b) {
+  const int x = *(const int *)a, y = *(const int *)b;
+  return (x > y) - (x < y);
+}
+
+/* R-MAT 2^scale x 2^scale with 16 * 2^scale edges: per edge and level a
+ * 16-bit draw picks a quadrant with thresholds (a, a+b, a+b+c) = (.57, .76,
+ * .95); duplicates merged, columns ascending, values u01(mix(kv + r*M + c)).
+ * Arrays are malloc'd (free with oracle_free).  Returns 0 or -1. */
+int oracle_gen_rmat(int scale, uint64_t seed, int *M_out, int **row_ptr, int **col,
+                    float **val, int *nnz_out) {
+  if (scale < 1 || scale > 28) return fail(-1, "rmat scale out of [1, 28]");
+  const int64_t M = (int64_t)1 << scale, E = 16 * M;
+  const uint32_t ta = 37355, tb = 49807, tc = 62259;
+  const uint64_t ke = og_key(seed, 3), kv = og_key(seed, 2);
+  int *er = (int *)malloc(sizeof(int) * (size_t)E), *ec = (int *)malloc(sizeof(int) * (size_t)E);
+  int *cnt = (int *)calloc((size_t)M + 1, sizeof(int));
+  int64_t *start = (int64_t *)malloc(sizeof(int64_t) * ((size_t)M + 1));
+  int *bucket = (int *)malloc(sizeof(int) * (size_t)E);
+  int64_t *uniq = (int64_t *)malloc(sizeof(int64_t) * ((size_t)M + 1));
+  if (!er || !ec || !cnt || !start || !bucket || !uniq) {
+    free(er); free(ec); free(cnt); free(start); free(bucket); free(uniq);
+    return fail(-1, "out of host memory");
+  }
+#pragma omp parallel for schedule(static)
+  for (int64_t e = 0; e < E; ++e) {
+    uint32_t r = 0, c = 0;
+    uint64_t bits = 0;
+    for (int l = 0; l < scale; ++l) {
+      if ((l & 3) == 0) bits = og_mix(ke + (uint64_t)e * 8 + (uint64_t)(l >> 2));
+      const uint32_t u = (uint32_t)(bits & 0xFFFF);
+      bits >>= 16;
+      r = (r << 1) | (u >= tb ? 1u : 0u);
+      c = (c << 1) | (((u >= ta && u < tb) || u >= tc) ? 1u : 0u);
+    }
+    er[e] = (int)r;
+    ec[e] = (int)c;
+  }
+#pragma omp parallel for schedule(static)
+  for (int64_t e = 0; e < E; ++e) __atomic_fetch_add(&cnt[er[e] + 1], 1, __ATOMIC_RELAXED);
+  start[0] = 0;
+  for (int64_t r = 0; r < M; ++r) start[r + 1] = start[r] + cnt[r + 1];
+  memset(cnt, 0, sizeof(int) * ((size_t)M + 1));
+#pragma omp parallel for schedule(static)
+  for (int64_t e = 0; e < E; ++e) {
+    const int r = er[e];
+    const int pos = __atomic_fetch_add(&cnt[r], 1, __ATOMIC_RELAXED);
+    bucket[start[r] + pos] = ec[e];
+  }
+  free(er);
+  free(ec);
+  uniq[0] = 0;
+#pragma omp parallel for schedule(dynamic, 1024)
+  for (int64_t r = 0; r < M; ++r) {
+    int *b = bucket + start[r];
+    const int64_t n = start[r + 1] - start[r];
+    qsort(b, (size_t)n, sizeof(int), og_cmp_int);
+    int64_t u = 0;
+    for (int64_t i = 0; i < n; ++i)
+      if (i == 0 || b[i] != b[i - 1]) b[u++] = b[i];
+    uniq[r + 1] = u;
+  }
+  for (int64_t r = 0; r < M; ++r) uniq[r + 1] += uniq[r];
+  if (uniq[M] > INT32_MAX) {
+    free(cnt); free(start); free(bucket); free(uniq);
+    return fail(-1, "rmat nnz exceeds int32");
+  }
+  const int nnz = (int)uniq[M];
+  int *rp = (int *)malloc(sizeof(int) * ((size_t)M + 1));
+  int *cc = (int *)malloc(sizeof(int) * (size_t)(nnz ? nnz : 1));
+  float *vv = (float *)malloc(sizeof(float) * (size_t)(nnz ? nnz : 1));
+  if (!rp || !cc || !vv) {
+    free(rp); free(cc); free(vv); free(cnt); free(start); free(bucket); free(uniq);
+    return fail(-1, "out of host memory");
+  }
+#pragma omp parallel for schedule(dynamic, 1024)
+  for (int64_t r = 0; r < M; ++r) {
+    rp[r] = (int)uniq[r];
+    for (int64_t t = 0; t < uniq[r + 1] - uniq[r]; ++t) {
+      const int c = bucket[start[r] + t];
+      cc[uniq[r] + t] = c;
+      vv[uniq[r] + t] = og_u01f(og_mix(kv + (uint64_t)r * (uint64_t)M + (uint64_t)c));
+    }
+  }
+  rp[M] = nnz;
+  free(cnt); free(start); free(bucket); free(uniq);
+  *M_out = (int)M;
+  *row_ptr = rp;
+  *col = cc;
+  *val = vv;
+  *nnz_out = nnz;
+  return 0;
+}

@@ -68,6 +68,10 @@ def lib():
         L.oracle_vcsr_spmm.argtypes = [C.POINTER(_VCSR), _f32p, C.c_int, _f32p]
         L.oracle_vcsr_free.argtypes = [C.POINTER(_VCSR)]
         L.oracle_free.argtypes = [C.c_void_p]
+        L.oracle_gen_dense.argtypes = [_f32p, C.c_int64, C.c_int64, C.c_uint64, C.c_float,
+                                       C.c_float]
+        L.oracle_gen_rmat.argtypes = [C.c_int, C.c_uint64, _i32p, C.POINTER(_i32p),
+                                      C.POINTER(_i32p), C.POINTER(_f32p), _i32p]
         L.oracle_max_threads.restype = C.c_int
         _LIB = L
     return _LIB
@@ -88,6 +92,27 @@ def _take(ptr, n, dtype, free):
         out = np.ctypeslib.as_array(ptr, shape=(n,)).astype(dtype, copy=True)
     free(C.cast(ptr, C.c_void_p))
     return out
+
+
+def gen_dense(rows, cols, seed, lo=-1.0, hi=1.0):
+    """The engine's seeded dense fill (vcsr_gen_dense), restated on the CPU."""
+    out = np.empty((rows, cols), np.float32)
+    lib().oracle_gen_dense(_p(out, _f32p), rows, cols, seed, lo, hi)
+    return out
+
+
+def gen_rmat(scale, seed=0):
+    """The engine's R-MAT matrix (gen_rmat), restated on the CPU ->
+    (M, row_ptr, col, val)."""
+    L = lib()
+    M, Z = C.c_int(), C.c_int()
+    r, c, v = _i32p(), _i32p(), _f32p()
+    rc = L.oracle_gen_rmat(scale, seed, C.byref(M), C.byref(r), C.byref(c), C.byref(v),
+                           C.byref(Z))
+    if rc:
+        raise OracleError(rc, L.oracle_last_error().decode())
+    return (M.value, _take(r, M.value + 1, np.int32, L.oracle_free),
+            _take(c, Z.value, np.int32, L.oracle_free), _take(v, Z.value, np.float32, L.oracle_free))
 
 
 def read_mtx(path):

@@ -211,6 +211,14 @@ def test_cli_drop_in(tmp_path):
     g = subprocess.run([exe, "--gen", "fem", "--size", "3000", "--O", "32", "--algo", "vcsr",
                         "--repeat", "2"], capture_output=True, text=True, timeout=120)
     assert g.returncode == 0 and "VCSR:" in g.stdout.splitlines()[-1]
+    # aspt names the engine kernels it runs; vcsr_tcseg runs the segment path
+    for algo, tag, what in (("aspt", "ASPT:", "1 row/vector"),
+                            ("vcsr_tcseg", "VCSR_TCSEG:", "split-TF32")):
+        g = subprocess.run([exe, "--gen", "fem", "--size", "3000", "--O", "64", "--algo", algo,
+                            "--repeat", "2", "--check"], capture_output=True, text=True,
+                           timeout=120)
+        assert g.returncode == 0, g.stderr
+        assert tag in g.stdout.splitlines()[-1] and what in g.stdout
     bad = subprocess.run([exe, "--mtx", "/nonexistent.mtx", "--O", "8"], capture_output=True,
                          text=True, timeout=60)
     assert bad.returncode != 0 and "Failed to open MTX" in bad.stderr

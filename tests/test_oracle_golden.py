@@ -153,3 +153,19 @@ def test_oracle_matches_reference_on_random_matrices():
         mine = oracle.csr_to_vcsr(M, N, rp, cc, vv, segw, bundle)
         ok, k = vcsr_equal_canonical(mine, ref)
         assert ok, (seed, k)
+
+
+def test_reference_arm_generators_match_the_library():
+    """The oracle's restatement of the seeded inputs (the reference arm builds
+    them without loading the engine) gives the engine generator's R-MAT matrix
+    and dense B bit for bit."""
+    import vcsr_b200 as V
+    for scale, seed in ((10, 0), (13, 3)):
+        M, rp, col, val = oracle.gen_rmat(scale, seed)
+        ref = V.gen_csr("rmat", seed, scale)
+        assert M == ref.M
+        assert np.array_equal(rp, ref.row_ptr) and np.array_equal(col, ref.col)
+        assert np.array_equal(val.view(np.int32), ref.val.view(np.int32))
+    for rows, cols, seed, lo in ((1000, 37, 1000, -1.0), (513, 256, 7, 0.0)):
+        assert np.array_equal(oracle.gen_dense(rows, cols, seed, lo, 1.0).view(np.int32),
+                              V.gen_dense_host(rows, cols, seed, lo, 1.0).view(np.int32))

@@ -7,11 +7,15 @@
 // [--seed s] for synthetic matrices, --gpus N for row panels on N GPUs,
 // --check for a relative-L2 comparison against cuSPARSE.
 //
-// Algorithms: cusparse (vendor), csr (row-wise CSR kernel; "aspt" is an
-// alias: its warp-per-row scheme is the CSR kernel's), vcsr (the
-// row-stationary engine), vcsr_seg / vcsr_baseline (race-free kernel on the
-// segment-major VCSRSpMM built on the GPU), all.  vcsr_naive and fast are
-// reported as not provided (see the design notes).
+// Algorithms: cusparse (vendor), csr (row-wise CSR kernel), aspt (the
+// engine at one row per vector: a sub-warp per short row, a whole warp with
+// xor-shuffle sums per long row and long rows split over several warps --
+// the warp-per-row scheme of src/aspt.cu:38-142 without its O % 64 limit),
+// vcsr (the row-stationary engine), vcsr_seg / vcsr_baseline (race-free
+// kernel on the segment-major VCSRSpMM built on the GPU), vcsr_tc (dense
+// 16x16 blocks in TF32), vcsr_tcseg (column runs on the tensor cores at FP32
+// accuracy), all.  vcsr_naive and fast are reported as not provided (see the
+// design notes).
 #include <cuda_runtime.h>
 #include <getopt.h>
 
@@ -33,7 +37,7 @@ void usage() {
          " --O 128 [options]\n");
   printf("Options: --segw w --bundle b --tileK t --repeat r --algo a --size s --seed s"
          " --gpus n --check --mtx-banner\n");
-  printf("Algorithms: cusparse, csr, vcsr, vcsr_seg, vcsr_baseline, aspt, all\n");
+  printf("Algorithms: cusparse, csr, aspt, vcsr, vcsr_seg, vcsr_baseline, vcsr_tc, vcsr_tcseg, all\n");
 }
 
 #define CK(x)                                                              \
@@ -262,12 +266,40 @@ int main(int argc, char **argv) {
              fetch());
     }
   }
-  if (all || algo == "csr" || algo == "aspt") {
+  if (all || algo == "csr") {
     double ms = timed([&] {
       VK(vcsr_csr_spmm(csr.M, d_rp, d_col, d_val, dB, O, dC, st));
     }, false);
     report("CSR (row-wise)", "CSR", ms, "warp-per-row CSR", fetch());
   }
+  // a plan of the engine with the given flags and vector height; its note
+  // names the kernels that ran
+  auto run_plan = [&](const char *name, const char *tag, int flags, int vec_rows,
+                      const char *what) {
+    vcsr_plan_params p;
+    vcsr_plan_params_default(&p);
+    p.segw = segw; p.bundle = bundle; p.tileK = tileK; p.max_O = std::max(O, 512);
+    p.flags = flags;
+    p.vec_rows = vec_rows;
+    vcsr_plan *plan = nullptr;
+    vcsr_csr view = as_view(csr);
+    VK(vcsr_plan_create(&view, VCSR_HOST, &p, &plan, st));
+    vcsr_plan_info info{};
+    VK(vcsr_plan_get_info(plan, &info));
+    int launches = 0;
+    double ms = timed([&] { VK(vcsr_spmm(plan, dB, O, dC, O, O, st, &launches)); }, false);
+    VK(vcsr_plan_check(plan, st));
+    char note[320];
+    snprintf(note, sizeof note,
+             "%s,vec_rows=%d,units=%d,split=%d,long=%d,tc_nnz=%lld,launches=%d,build=%.1f ms",
+             what, info.vec_rows, info.num_units, info.num_split_units, info.num_long_units,
+             (long long)info.panel_nnz, launches, info.build_ms);
+    report(name, tag, ms, note, fetch());
+    vcsr_plan_destroy(plan);
+  };
+  if (all || algo == "aspt")
+    run_plan("ASPT (engine)", "ASPT", 0, 1,
+             "engine panels at 1 row/vector: sub-warp per short row, warp per long row");
   if (all || algo == "vcsr") {
     vcsr_plan_params p;
     vcsr_plan_params_default(&p);
@@ -315,6 +347,15 @@ int main(int argc, char **argv) {
                info.num_panel_blocks, (long long)info.panel_nnz, info.vec_rows);
       report("VCSR_TC (TF32)", "VCSR_TC", ms, note, fetch());
       vcsr_plan_destroy(plan);
+    }
+  }
+  if (all || algo == "vcsr_tcseg") {  // column runs on the tensor cores, FP32 accuracy
+    if (O % 4) {
+      printf("%-16s %10s %12s (tensor-core segments need O %% 4 == 0)\n", "VCSR_TCSEG", "N/A",
+             "N/A");
+    } else {
+      run_plan("VCSR_TCSEG", "VCSR_TCSEG", VCSR_PLAN_TC_SEGMENTS, 0,
+               "tcgen05 split-TF32 column runs + FP32 residual");
     }
   }
   for (const char *na : {"vcsr_naive", "fast"})

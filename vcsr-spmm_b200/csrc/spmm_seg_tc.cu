@@ -22,7 +22,7 @@
 // between the copy and the MMAs (converter warps), so B and A are read from
 // memory once, as stored.
 //
-// B tiles come by TMA: per 8 rows one box of 8 rows x 32 floats x 4 chunks
+// B tiles come by TMA: per piece one box of L rows x 32 floats x 4 chunks
 // (a 3-D view of B when O is a multiple of 32, else four 2-D boxes) in the
 // 128-byte swizzle with 32-byte atoms that the MN-major TF32 operand needs;
 // rows past N read as zeros.  The A tile is one bulk copy.  Roles (320
@@ -79,8 +79,15 @@ __device__ __forceinline__ void split4(float4 &x, float4 &lo) {
   x = make_float4(hx, hy, hz, hw);
 }
 
+// B's tensor maps, one per piece height L = 8, 16, 24, 32: a piece's B rows
+// come in with one copy (3-D view: box {32, L, 4}; 2-D view: four boxes
+// {32, L}), chunk-major, chunk c at c * L * 128 bytes.
+struct SegMaps {
+  CUtensorMap m[kSegPieceRows / 8];
+};
+
 __global__ void __launch_bounds__(kSegThreads, kSegCtas)
-    seg_tc_kernel(const SegView V, const __grid_constant__ CUtensorMap tmB) {
+    seg_tc_kernel(const SegView V, const __grid_constant__ SegMaps maps) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   unsigned char *base = reinterpret_cast<unsigned char *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -161,17 +168,14 @@ __global__ void __launch_bounds__(kSegThreads, kSegCtas)
           }
           meta[s] = pc.y | (q == q0 ? 256 : 0) | (q == q1 - 1 ? 512 : 0);
           unsigned char *st = stage + (size_t)s * kSegStageBytes;
-          const int groups = pc.y >> 3;
-          mbar_add_tx(full + s, (uint32_t)(groups * kGroupBytes + pc.y * 64));
-          for (int j = 0; j < groups; ++j) {
-            if (V.slab3d) {
-              tma_load_3d(st + j * kGroupBytes, &tmB, 0, pc.x + 8 * j, oc * 4, full + s);
-            } else {
+          const CUtensorMap *tm = &maps.m[(pc.y >> 3) - 1];
+          mbar_add_tx(full + s, (uint32_t)(pc.y * 512 + pc.y * 64));
+          if (V.slab3d) {
+            tma_load_3d(st, tm, 0, pc.x, oc * 4, full + s);
+          } else {
 #pragma unroll
-              for (int c = 0; c < 4; ++c)
-                tma_load_2d(st + j * kGroupBytes + c * 1024, &tmB, oc * 128 + 32 * c,
-                            pc.x + 8 * j, full + s);
-            }
+            for (int c = 0; c < 4; ++c)
+              tma_load_2d(st + c * pc.y * 128, tm, oc * 128 + 32 * c, pc.x, full + s);
           }
           bulk_load(st + 2 * kPieceB, V.a + (size_t)pc.z * 16, (uint32_t)(pc.y * 64), full + s);
           mbar_arrive(full + s);
@@ -251,10 +255,11 @@ __global__ void __launch_bounds__(kSegThreads, kSegCtas)
         const uint32_t bh = smem_u32(stage + (size_t)s * kSegStageBytes);
         const uint32_t bl = bh + kPieceB, ah = bh + 2 * kPieceB, al = ah + kPieceA;
         for (int h = 0; h < (L >> 3); ++h) {
-          // B: 32-float chunks 1024 bytes apart, 4-row swizzle atoms 512 apart;
-          // A: core matrices 128 bytes apart along N, 256 along K
-          const uint64_t bdh = smem_desc(bh + h * kGroupBytes, 1024, 512, 1);
-          const uint64_t bdl = smem_desc(bl + h * kGroupBytes, 1024, 512, 1);
+          // B: 32-float chunks L * 128 bytes apart, this K step's rows at
+          // h * 1024, 4-row swizzle atoms 512 apart; A: core matrices 128
+          // bytes apart along N, 256 along K
+          const uint64_t bdh = smem_desc(bh + h * 1024, L * 128, 512, 1);
+          const uint64_t bdl = smem_desc(bl + h * 1024, L * 128, 512, 1);
           const uint64_t adh = smem_desc(ah + h * 512, 256, 128, 0);
           const uint64_t adl = smem_desc(al + h * 512, 256, 128, 0);
           mma_tf32(dt, bdh, adh, first ? 0u : 1u);
@@ -347,30 +352,34 @@ vcsr_status launch_seg_tc(const SegView &V0, const float *B, int N, int ldb, flo
                 "tensor-core segments need O and ldb multiples of 4 and a 16-byte aligned B");
   EncodeTiledFn enc;
   VCSR_TRY(tensor_map_encoder(&enc));
-  CUtensorMap tm;
+  SegMaps maps;
   // O a multiple of 32: the 3-D view {32 floats, N rows, O/32 chunks} (strides
-  // ldb*4 and 128 bytes) with {32, 8, 4} boxes lands one K step's four chunks
+  // ldb*4 and 128 bytes) with {32, L, 4} boxes lands a piece's four chunks
   // with one copy; chunks past O/32 read as zeros.  Otherwise the 2-D view
-  // {O, N} with 32 x 8 boxes zero-fills past O.
+  // {O, N} with 32 x L boxes zero-fills past O.
   const bool slab3d = (O % 32) == 0;
   const cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r;
-  if (slab3d) {
-    const cuuint64_t dims[3] = {32, (cuuint64_t)N, (cuuint64_t)(O / 32)};
-    const cuuint64_t strides[2] = {(cuuint64_t)ldb * 4, 128};
-    const cuuint32_t box[3] = {32, 8, 4};
-    r = enc(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void *)B, dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  } else {
-    const cuuint64_t dims[2] = {(cuuint64_t)O, (cuuint64_t)N};
-    const cuuint64_t strides[1] = {(cuuint64_t)ldb * 4};
-    const cuuint32_t box[2] = {32, 8};
-    r = enc(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)B, dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  for (int k = 0; k < kSegPieceRows / 8; ++k) {
+    const cuuint32_t L = (cuuint32_t)(8 * (k + 1));
+    CUresult r;
+    if (slab3d) {
+      const cuuint64_t dims[3] = {32, (cuuint64_t)N, (cuuint64_t)(O / 32)};
+      const cuuint64_t strides[2] = {(cuuint64_t)ldb * 4, 128};
+      const cuuint32_t box[3] = {32, L, 4};
+      r = enc(&maps.m[k], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void *)B, dims, strides, box,
+              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    } else {
+      const cuuint64_t dims[2] = {(cuuint64_t)O, (cuuint64_t)N};
+      const cuuint64_t strides[1] = {(cuuint64_t)ldb * 4};
+      const cuuint32_t box[2] = {32, L};
+      r = enc(&maps.m[k], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)B, dims, strides, box,
+              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    }
+    if (r != CUDA_SUCCESS)
+      return fail(VCSR_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   }
-  if (r != CUDA_SUCCESS) return fail(VCSR_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   SegView V = V0;
   V.slab3d = slab3d ? 1 : 0;
   V.O = O;
@@ -389,7 +398,7 @@ vcsr_status launch_seg_tc(const SegView &V0, const float *B, int N, int ldb, flo
   const long long items = (long long)V.n_rb * V.n_ochunks;
   long long grid = (long long)sms * kSegCtas;  // resident CTAs (shared memory)
   if (grid > items) grid = items;
-  seg_tc_kernel<<<(int)grid, kSegThreads, smem, st>>>(V, tm);
+  seg_tc_kernel<<<(int)grid, kSegThreads, smem, st>>>(V, maps);
   VCSR_CUDA(cudaGetLastError());
   if (launches) *launches = 1;
   return VCSR_OK;
