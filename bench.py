@@ -414,6 +414,9 @@ def measure(args, ctx, workload, steps, warmup, extras):
     global_M = D.sum_over_ranks(dist, csr.M, dev) if world > 1 else csr.M
     lo = 0.0 if cfg == "rmat" else -1.0
     tf32 = workload in TF32_WORKLOADS
+    if not ctx.get("warm"):  # first use of the builder kernels (module load): untimed
+        V.Plan(V.gen_csr("fem", 0, 600), tf32_panels=tf32)
+        ctx["warm"] = True
     plan = V.Plan(csr, segw=4, bundle=32, max_O=max(O, 512), tf32_panels=tf32, target_O=O)
     info = plan.info()
 

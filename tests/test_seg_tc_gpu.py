@@ -130,6 +130,17 @@ def test_save_load_and_host_entry_point(tmp_path):
     assert rel_l2(Ch, ref) <= TOL
 
 
+def test_no_run_long_enough():
+    """A plan whose runs are all shorter than seg_min_run has no pieces: the
+    FP32 kernel computes everything."""
+    csr = V.gen_csr("uniform", 0, 256)
+    plan = V.Plan(csr, tc_segments=True, seg_min_run=1000)
+    assert plan.info()["num_seg_pieces"] == 0
+    B = V.gen_dense_host(csr.N, 16, 4)
+    ref = oracle.csr_spmm_f64(csr.M, csr.row_ptr, csr.col, csr.val, B)
+    assert rel_l2(product(plan, B, csr.M), ref) <= TOL
+
+
 def test_refusals():
     csr = V.gen_csr("fem", 0, 600)
     plan = V.Plan(csr, tc_segments=True)

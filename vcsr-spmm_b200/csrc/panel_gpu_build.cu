@@ -322,41 +322,57 @@ __global__ void positive_flags_kernel(const int *__restrict__ a, int64_t n, int 
 }
 
 // ------------------------------------------------- vector height
+// The sampled windows: window of sample s = s * windows / samples (16 rows
+// from row 16 * window); cnt[s] = its entries.
+__global__ void sample_counts_kernel(const int *__restrict__ rp, int M, int64_t windows,
+                                     int samples, int *cnt) {
+  GRID_STRIDE(s, samples) {
+    const int64_t w = s * windows / samples;
+    const int r0 = (int)(w * 16), r1 = min(M, r0 + 16);
+    cnt[s] = rp[r1] - rp[r0];
+  }
+}
+
 // acc[0] = entries of the sampled windows, acc[1 + j] = the sum of the union
-// sizes of their vectors at R = 1, 2, 4, 8, 16 (vectors aligned to the
-// window, which starts at a multiple of 16 rows).  An entry counts towards
-// its vector's union when no earlier row of the vector holds its (column,
-// occurrence) key.
+// sizes of their vectors at R = 2, 4, 8, 16 (vectors aligned to the window,
+// which starts at a multiple of 16 rows).  An entry counts towards its
+// vector's union when no earlier row of the vector holds its (column,
+// occurrence) key.  One thread per sampled entry (off = exclusive prefix of
+// the windows' entries), so a window of long rows spreads over many blocks.
 __global__ void sample_unions_kernel(const int *__restrict__ rp, const int *__restrict__ col,
                                      int M, int64_t windows, int samples,
+                                     const int *__restrict__ off, int total,
                                      unsigned long long *acc) {
   __shared__ unsigned long long part[5][kThreads / 32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   unsigned long long loc[5] = {0, 0, 0, 0, 0};  // entries, R = 2, 4, 8, 16
-  for (int s = blockIdx.x; s < samples; s += gridDim.x) {
-    const int64_t w = (int64_t)s * windows / samples;
-    const int r0 = (int)(w * 16), r1 = min(M, r0 + 16);
-    const int p0 = rp[r0], p1 = rp[r1];
-    for (int p = p0 + threadIdx.x; p < p1; p += blockDim.x) {
-      int r = r0;
-      while (rp[r + 1] <= p) ++r;
-      const int c = col[p];
-      const int occ = p - lower_idx(col, rp[r], p, c);
-      unsigned present = 0;
-      for (int rr = r0; rr < r; ++rr) {
-        const int b = rp[rr], e = rp[rr + 1];
-        const int lo = lower_idx(col, b, e, c);
-        const int hi = upper_idx(col, lo, e, c);
-        if (hi - lo > occ) present |= 1u << (rr - r0);
-      }
-      loc[0] += 1;
+  GRID_STRIDE(i, total) {
+    int lo = 0, hi = samples;  // the sample holding entry i: last s with off[s] <= i
+    while (hi - lo > 1) {
+      const int m = (lo + hi) >> 1;
+      if (off[m] <= i) lo = m; else hi = m;
+    }
+    const int64_t w = (int64_t)lo * windows / samples;
+    const int r0 = (int)(w * 16);
+    const int p = rp[r0] + (int)(i - off[lo]);
+    int r = r0;
+    while (rp[r + 1] <= p) ++r;
+    const int c = col[p];
+    const int occ = p - lower_idx(col, rp[r], p, c);
+    unsigned present = 0;
+    for (int rr = r0; rr < r; ++rr) {
+      const int b = rp[rr], e = rp[rr + 1];
+      const int l0 = lower_idx(col, b, e, c);
+      const int h0 = upper_idx(col, l0, e, c);
+      if (h0 - l0 > occ) present |= 1u << (rr - r0);
+    }
+    loc[0] += 1;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int R = 2 << j;
-        const int vs = ((r - r0) / R) * R;
-        const unsigned mask = ((1u << (r - r0)) - 1u) & ~((1u << vs) - 1u);
-        if (!(present & mask)) loc[1 + j] += 1;
-      }
+    for (int j = 0; j < 4; ++j) {
+      const int R = 2 << j;
+      const int vs = ((r - r0) / R) * R;
+      const unsigned mask = ((1u << (r - r0)) - 1u) & ~((1u << vs) - 1u);
+      if (!(present & mask)) loc[1 + j] += 1;
     }
   }
 #pragma unroll
@@ -536,12 +552,24 @@ __global__ void row_cut_kernel(const int *__restrict__ rp, int M, const long lon
 // each row's last entry), -1 for none.
 __global__ void panel_colmax_kernel(const int *__restrict__ rp, const int *__restrict__ col,
                                     int M, const int *__restrict__ bounds, int n, int *col_max) {
-  GRID_STRIDE(r, M) {
-    const int e = rp[r + 1];
-    if (e == rp[r]) continue;
-    int j = 0;
-    while (j + 1 < n && r >= bounds[j + 1]) ++j;
-    atomicMax(col_max + j, col[e - 1]);
+  // whole warps run the loop (rows past M count as empty), so that a warp
+  // whose rows share a panel reduces before its one atomic
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t Mw = ((int64_t)M + 31) & ~(int64_t)31;
+  for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < Mw; r += stride) {
+    int v = -1, j = 0;
+    if (r < M) {
+      const int e = rp[r + 1];
+      if (e > rp[r]) v = col[e - 1];
+      while (j + 1 < n && r >= bounds[j + 1]) ++j;
+    }
+    const int j0 = __shfl_sync(0xffffffffu, j, 0);
+    if (__all_sync(0xffffffffu, j == j0)) {
+      const int m = __reduce_max_sync(0xffffffffu, v);
+      if ((threadIdx.x & 31) == 0 && m >= 0) atomicMax(col_max + j0, m);
+    } else if (v >= 0) {
+      atomicMax(col_max + j, v);
+    }
   }
 }
 
@@ -662,10 +690,19 @@ vcsr_status choose_vec_rows_device(const vcsr_csr &w, int sms, Scratch &sc, int 
   *R_out = 1;
   if (samples == 0) return VCSR_OK;
   unsigned long long *acc = nullptr;
+  int *cnt = nullptr, *off = nullptr;
   VCSR_TRY(sc.get(&acc, 5));
+  VCSR_TRY(sc.get(&cnt, samples));
+  VCSR_TRY(sc.get(&off, (int64_t)samples + 1));
   VCSR_CUDA(cudaMemsetAsync(acc, 0, 5 * sizeof(unsigned long long), sc.st));
-  sample_unions_kernel<<<(unsigned)std::min(samples, sms * 8), kThreads, 0, sc.st>>>(
-      w.row_ptr, w.col, w.M, windows, samples, acc);
+  sample_counts_kernel<<<grid_for(samples), kThreads, 0, sc.st>>>(w.row_ptr, w.M, windows,
+                                                                   samples, cnt);
+  VCSR_CUDA(cudaGetLastError());
+  VCSR_TRY(scan_exclusive<int>(cnt, off, samples, off + samples, sc));
+  int total = 0;
+  VCSR_TRY(read1(&total, off + samples, sc.st));
+  sample_unions_kernel<<<grid_for(total), kThreads, 0, sc.st>>>(
+      w.row_ptr, w.col, w.M, windows, samples, off, total, acc);
   VCSR_CUDA(cudaGetLastError());
   unsigned long long h[5];
   VCSR_CUDA(cudaMemcpyAsync(h, acc, sizeof h, cudaMemcpyDeviceToHost, sc.st));
@@ -797,8 +834,10 @@ vcsr_status build_plan_layout_device(vcsr_plan *p, const vcsr_csr &d, int sms,
     VCSR_TRY(sc.get(&uc16, U16));
     VCSR_TRY(sc.get(&uv16, (int64_t)U16 * 16));
     VCSR_TRY(sc.get(&um16, U16));
-    VCSR_CUDA(cudaMemsetAsync(uv16, 0, sizeof(float) * 16 * (size_t)(U16 > 0 ? U16 : 1), st));
-    VCSR_CUDA(cudaMemsetAsync(um16, 0, sizeof(unsigned) * (size_t)(U16 > 0 ? U16 : 1), st));
+    if (U16 > 0) {
+      VCSR_CUDA(cudaMemsetAsync(uv16, 0, sizeof(float) * 16 * (size_t)U16, st));
+      VCSR_CUDA(cudaMemsetAsync(um16, 0, sizeof(unsigned) * (size_t)U16, st));
+    }
     vec_ptr_kernel<<<grid_for((int64_t)V16 + 1), kThreads, 0, st>>>(d.row_ptr, F, M, 16, V16,
                                                                      vp16);
     place_kernel<<<grid_for(nnz), kThreads, 0, st>>>(d.row_ptr, d.col, d.val, row_of, F, M, nnz,
@@ -841,8 +880,8 @@ vcsr_status build_plan_layout_device(vcsr_plan *p, const vcsr_csr &d, int sms,
     VCSR_TRY(sc.get(&runs, n_runs));
     VCSR_TRY(dmalloc(&p->d_seg_pieces, n_pieces));
     VCSR_TRY(dmalloc(&p->d_seg_a, (int64_t)seg_rows * 16));
-    VCSR_CUDA(cudaMemsetAsync(p->d_seg_a, 0, sizeof(float) * 16 * (size_t)(seg_rows > 0 ? seg_rows : 1),
-                              st));
+    if (seg_rows > 0)
+      VCSR_CUDA(cudaMemsetAsync(p->d_seg_a, 0, sizeof(float) * 16 * (size_t)seg_rows, st));
     seg_runs_kernel<<<grid_for(V16), kThreads, 0, st>>>(
         vp16, uc16, uv16, um16, V16, min_run, 2, nullptr, nullptr, nullptr, nullptr, run_off,
         piece_off, row_off, runs, p->d_seg_pieces, p->d_seg_a);
