@@ -375,7 +375,25 @@ def library_peers(torch, V, csr, dB32, O, dC, flush, stream, flops, value, reps)
     ts = timed_events(torch, lambda: V.run_csr_spmm_gpu(csr.M, d.row_ptr, d.col, d.val, dB32,
                                                         O, dCp, stream), reps, stream, flush)
     peers["csr_rowwise_gflops"] = round(flops / (np.mean(ts) * 1e-3) / 1e9, 2)
-    del d, dCp
+    # The reference's launcher run_vcsr_spmm_gpu (src/kernels.cu:120-167) on
+    # the engine: the plan built on the GPU from the segment-major VCSR (per
+    # call in the launcher, outside its timed region as the reference's upload
+    # is), then C += A*B timed; and the segment-major kernel on the VCSR itself.
+    v = V.csr_to_vcsr_spmm(d, 4, 32, stream=stream)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    pv = V.Plan.from_vcsr(v, max_O=max(O, 512), stream=stream)
+    build_ms = (time.perf_counter() - t0) * 1e3
+    ts = timed_events(torch, lambda: pv.spmm(dB32, dCp, stream=stream, accumulate=True), reps,
+                      stream, flush)
+    ts_seg = timed_events(torch, lambda: V.run_vcsr_spmm_segmented_gpu(v, dB32, O, 64, dCp,
+                                                                       stream),
+                          min(reps, 5), stream, flush)
+    peers["drop_in_run_vcsr_spmm_gpu"] = {
+        "gflops": round(flops / (np.mean(ts) * 1e-3) / 1e9, 2),
+        "plan_from_vcsr_ms": round(build_ms, 1),
+        "segmented_kernel_gflops": round(flops / (np.mean(ts_seg) * 1e-3) / 1e9, 2)}
+    del pv, v, d, dCp
     return peers
 
 

@@ -244,6 +244,18 @@ void vcsr_plan_params_default(vcsr_plan_params *p);
 vcsr_status vcsr_plan_create(const vcsr_csr *csr, int csr_where,
                              const vcsr_plan_params *params, vcsr_plan **out,
                              vcsr_stream_t stream);
+/* Build a plan for the matrix a segment-major VCSR holds (the reference's
+ * VCSRSpMM, include/vcsr.hpp:12-23, as host or device arrays by `where`):
+ * the slots with a row >= 0 and an lcol >= 0 become entries (row, column
+ * group_seg_base + lcol, value) on the GPU, rows in slot order, and the plan
+ * is built from them as vcsr_plan_create builds a device CSR.  This lets a
+ * caller of the reference's launcher, which receives this format
+ * (src/kernels.cu:120-167), run the engine.  Errors: VCSR_ERR_INVALID when
+ * group_ptr does not match group_depth * bundle and num_slots or a segment
+ * base is outside [0, N); VCSR_ERR_RANGE for a row outside [-1, M) or an
+ * lcol outside [-1, segw) or past column N. */
+vcsr_status vcsr_plan_from_vcsr(const vcsr_vcsr *v, int where, const vcsr_plan_params *params,
+                                vcsr_plan **out, vcsr_stream_t stream);
 vcsr_status vcsr_plan_get_info(const vcsr_plan *plan, vcsr_plan_info *info);
 /* Host copy of the plan's segment-major VCSR (needs VCSR_PLAN_REFERENCE_FORMAT). */
 vcsr_status vcsr_plan_export(const vcsr_plan *plan, vcsr_vcsr *host_out);
@@ -270,6 +282,14 @@ vcsr_status vcsr_plan_load(const char *path, vcsr_plan **out, vcsr_stream_t stre
 vcsr_status vcsr_spmm(const vcsr_plan *plan, const float *dB, int ldb,
                       float *dC, int ldc, int O, vcsr_stream_t stream,
                       int *launches);
+/* C += A * B: vcsr_spmm's product added into C, the contract of the
+ * reference's launcher (src/kernels.cu:120-167, whose kernel adds into a C
+ * the caller zeroed).  Each value of C is read and written once, by one
+ * thread (no atomics: the result does not depend on the schedule); rows of A
+ * without entries leave C as it was.  Same other rules as vcsr_spmm. */
+vcsr_status vcsr_spmm_accumulate(const vcsr_plan *plan, const float *dB, int ldb,
+                                 float *dC, int ldc, int O, vcsr_stream_t stream,
+                                 int *launches);
 
 /* Row panels of a plan (about equal nnz; at most 8), for callers that
  * schedule the product themselves, e.g. behind a chunked broadcast of B: on

@@ -94,15 +94,18 @@ def test_plan_export_is_reference_format():
 
 
 @pytest.mark.parametrize("O", [1, 8, 33, 128])
-def test_segmented_spmm_drop_in(O):
-    """run_vcsr_spmm_gpu semantics: C += A*B on the segment-major format."""
+@pytest.mark.parametrize("launch", ["run_vcsr_spmm_gpu", "run_vcsr_spmm_segmented_gpu"])
+def test_segmented_spmm_drop_in(O, launch):
+    """run_vcsr_spmm_gpu semantics, C += A*B, for the launcher on the engine
+    and for the segment-major kernel on the format itself."""
     csr = V.gen_csr("fem", 0, 3001)  # N % segw != 0: the last segment is ragged
     B = V.gen_dense_host(csr.N, O, 4)
     d = V.DeviceCSR(csr)
     v = V.csr_to_vcsr_spmm(d, 4, 32)
     dB = torch.from_numpy(B).cuda()
     dC = torch.zeros(csr.M, O, device="cuda")
-    V.run_vcsr_spmm_gpu(v, dB, O, 64, dC)
+    run = getattr(V, launch)
+    run(v, dB, O, 64, dC)
     torch.cuda.synchronize()
     ref = oracle.csr_spmm_f64(csr.M, csr.row_ptr, csr.col, csr.val, B)
     assert rel_l2(dC.cpu().numpy(), ref) <= 1e-5
@@ -110,7 +113,7 @@ def test_segmented_spmm_drop_in(O):
     seq = oracle.vcsr_spmm(h, B)  # the reference kernel's update, sequential
     assert rel_l2(dC.cpu().numpy(), seq) <= 1e-5
     # accumulate semantics: a second call doubles C
-    V.run_vcsr_spmm_gpu(v, dB, O, 64, dC)
+    run(v, dB, O, 64, dC)
     torch.cuda.synchronize()
     assert rel_l2(dC.cpu().numpy(), 2 * ref) <= 1e-5
 
@@ -211,9 +214,11 @@ def test_cli_drop_in(tmp_path):
     g = subprocess.run([exe, "--gen", "fem", "--size", "3000", "--O", "32", "--algo", "vcsr",
                         "--repeat", "2"], capture_output=True, text=True, timeout=120)
     assert g.returncode == 0 and "VCSR:" in g.stdout.splitlines()[-1]
-    # aspt names the engine kernels it runs; vcsr_tcseg runs the segment path
+    # aspt names the engine kernels it runs; vcsr_tcseg runs the segment path;
+    # fast runs the engine's 16-row condensed windows
     for algo, tag, what in (("aspt", "ASPT:", "1 row/vector"),
-                            ("vcsr_tcseg", "VCSR_TCSEG:", "split-TF32")):
+                            ("vcsr_tcseg", "VCSR_TCSEG:", "split-TF32"),
+                            ("fast", "FAST:", "vec_rows=16")):
         g = subprocess.run([exe, "--gen", "fem", "--size", "3000", "--O", "64", "--algo", algo,
                             "--repeat", "2", "--check"], capture_output=True, text=True,
                            timeout=120)

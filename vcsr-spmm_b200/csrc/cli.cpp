@@ -14,8 +14,11 @@
 // vcsr (the row-stationary engine), vcsr_seg / vcsr_baseline (race-free
 // kernel on the segment-major VCSRSpMM built on the GPU), vcsr_tc (dense
 // 16x16 blocks in TF32), vcsr_tcseg (column runs on the tensor cores at FP32
-// accuracy), all.  vcsr_naive and fast are reported as not provided (see the
-// design notes).
+// accuracy), fast / fastspmm (the row-window condensation of
+// src/fastspmm.cu:129-253 -- 16-row windows, the window's distinct columns
+// condensed, a dense 16-value tile per condensed column -- which is the
+// engine's vector panel at 16 rows per vector, computed in FP32), all.
+// vcsr_naive is reported as not provided.
 #include <cuda_runtime.h>
 #include <getopt.h>
 
@@ -37,7 +40,8 @@ void usage() {
          " --O 128 [options]\n");
   printf("Options: --segw w --bundle b --tileK t --repeat r --algo a --size s --seed s"
          " --gpus n --check --mtx-banner\n");
-  printf("Algorithms: cusparse, csr, aspt, vcsr, vcsr_seg, vcsr_baseline, vcsr_tc, vcsr_tcseg, all\n");
+  printf("Algorithms: cusparse, csr, aspt, vcsr, vcsr_seg, vcsr_baseline, vcsr_tc, vcsr_tcseg,"
+         " fast, all\n");
 }
 
 #define CK(x)                                                              \
@@ -358,8 +362,11 @@ int main(int argc, char **argv) {
                "tcgen05 split-TF32 column runs + FP32 residual");
     }
   }
-  for (const char *na : {"vcsr_naive", "fast"})
-    if (algo == na) printf("%-16s %10s %12s (not provided by this engine)\n", na, "N/A", "N/A");
+  if (all || algo == "fast" || algo == "fastspmm")
+    run_plan("FastSpMM (engine)", "FAST", 0, 16,
+             "16-row windows with condensed columns: engine panels at 16 rows/vector, FP32");
+  if (algo == "vcsr_naive")
+    printf("%-16s %10s %12s (not provided by this engine)\n", "vcsr_naive", "N/A", "N/A");
   printf("\n");
   for (auto &s : summary) printf("%s\n", s.c_str());
   cudaStreamDestroy(st);

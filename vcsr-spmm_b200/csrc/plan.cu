@@ -521,8 +521,13 @@ void vcsr_plan_destroy(vcsr_plan *p) {
   delete p;
 }
 
-vcsr_status vcsr_spmm(const vcsr_plan *p, const float *dB, int ldb, float *dC,
-                      int ldc, int O, vcsr_stream_t stream, int *launches) {
+namespace {
+
+// C = A * B, or C += A * B with `accumulate`: every kernel of the plan then
+// adds into C (the FP32 kernels load, add and store each finished value; the
+// tensor-core kernels add their product after the FP32 residual).
+vcsr_status spmm_impl(const vcsr_plan *p, const float *dB, int ldb, float *dC, int ldc, int O,
+                      vcsr_stream_t stream, int *launches, bool accumulate) {
   vcsr::clear_error();
   if (launches) *launches = 0;
   if (!p) return fail(VCSR_ERR_INVALID, "null plan");
@@ -536,9 +541,11 @@ vcsr_status vcsr_spmm(const vcsr_plan *p, const float *dB, int ldb, float *dC,
                 "O=%d exceeds the plan's max_O=%d (split rows need scratch)", O,
                 p->pstride);
   int n1 = 0, n2 = 0;
+  vcsr::PanelDevView pv = view(p);
+  pv.accumulate = accumulate ? 1 : 0;
   if (p->n_seg_rb > 0) {  // tensor-core segments; the residual (if any) first
     if (!p->seg_only)
-      VCSR_TRY(vcsr::launch_panel_spmm(view(p), false, dB, ldb, dC, ldc, O,
+      VCSR_TRY(vcsr::launch_panel_spmm(pv, false, dB, ldb, dC, ldc, O,
                                        (cudaStream_t)stream, &n1, p->side, p->fork, p->join));
     vcsr::SegView sv;
     sv.n_rb = p->n_seg_rb;
@@ -550,13 +557,13 @@ vcsr_status vcsr_spmm(const vcsr_plan *p, const float *dB, int ldb, float *dC,
     sv.col = p->d_seg_col;
     sv.val = p->d_seg_val;
     sv.M = p->M;
-    sv.accumulate = p->seg_only ? 0 : 1;
+    sv.accumulate = (p->seg_only && !accumulate) ? 0 : 1;
     sv.err = p->d_err;
     VCSR_TRY(vcsr::launch_seg_tc(sv, dB, p->N, ldb, dC, ldc, O, (cudaStream_t)stream, &n2));
     if (launches) *launches = n1 + n2;
     return VCSR_OK;
   }
-  VCSR_TRY(vcsr::launch_panel_spmm(view(p), false, dB, ldb, dC, ldc, O, (cudaStream_t)stream,
+  VCSR_TRY(vcsr::launch_panel_spmm(pv, false, dB, ldb, dC, ldc, O, (cudaStream_t)stream,
                                    &n1, p->side, p->fork, p->join));
   if (p->n_panel_rb > 0) {  // C += dense panels * B on the tensor cores
     vcsr::TcView tv;
@@ -572,6 +579,18 @@ vcsr_status vcsr_spmm(const vcsr_plan *p, const float *dB, int ldb, float *dC,
   }
   if (launches) *launches = n1 + n2;
   return VCSR_OK;
+}
+
+}  // namespace
+
+vcsr_status vcsr_spmm(const vcsr_plan *p, const float *dB, int ldb, float *dC,
+                      int ldc, int O, vcsr_stream_t stream, int *launches) {
+  return spmm_impl(p, dB, ldb, dC, ldc, O, stream, launches, false);
+}
+
+vcsr_status vcsr_spmm_accumulate(const vcsr_plan *p, const float *dB, int ldb, float *dC,
+                                 int ldc, int O, vcsr_stream_t stream, int *launches) {
+  return spmm_impl(p, dB, ldb, dC, ldc, O, stream, launches, true);
 }
 
 vcsr_status vcsr_plan_row_panels(const vcsr_plan *p, int *count, int *row0, int *row1,

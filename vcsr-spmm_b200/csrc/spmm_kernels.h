@@ -32,6 +32,7 @@ struct PanelDevView {
   int n_split_units = 0;
   int M = 0;
   int R = 1;
+  int accumulate = 0;  // C += A * B instead of C = A * B
 };
 
 // Element type of B: FP32 as stored, or 16-bit values widened to FP32 as they

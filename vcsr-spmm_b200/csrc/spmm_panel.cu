@@ -402,18 +402,28 @@ __device__ __forceinline__ void settle_rows(const PanelDevView &P, const TB *__r
   }
 }
 
+// One finished value of C: written (C = A * B), or with `accumulate` added
+// to what C holds (C += A * B, the contract of the reference's launcher,
+// src/kernels.cu:120-167, whose caller zeroes C).
+template <int VW>
+__device__ __forceinline__ void put_c(bool accumulate, float *p, typename VecT<VW>::T v) {
+  if (accumulate) v = VecT<VW>::add(VecT<VW>::ldcg(p), v);
+  VecT<VW>::stcs(p, v);
+}
+
 template <int R, int NV, int VW>
-__device__ __forceinline__ void store_rows(float *__restrict__ C, int ldc, int M, int row0,
-                                           const int (&kk)[NV], const bool (&ok)[NV],
+__device__ __forceinline__ void store_rows(const PanelDevView &P, float *__restrict__ C,
+                                           int ldc, int row0, const int (&kk)[NV],
+                                           const bool (&ok)[NV],
                                            const typename VecT<VW>::T (&out)[R][NV]) {
-  using V = VecT<VW>;
+  const bool accumulate = P.accumulate != 0;
 #pragma unroll
   for (int r = 0; r < R; ++r) {
     const int row = row0 + r;
-    if (row < M) {
+    if (row < P.M) {
 #pragma unroll
       for (int v = 0; v < NV; ++v)
-        if (ok[v]) V::stcs(C + (size_t)row * ldc + kk[v], out[r][v]);
+        if (ok[v]) put_c<VW>(accumulate, C + (size_t)row * ldc + kk[v], out[r][v]);
     }
   }
 }
@@ -428,7 +438,7 @@ __device__ __forceinline__ void cross_boundaries(int a, BatchCursor &bc, Acc<R, 
     typename VecT<VW>::T o[R][NV];
     acc.store(o);
     settle_rows<R, NV, VW, TB>(P, B, ldb, bc.vb, bc.ve, kk, ok, o);
-    store_rows<R, NV, VW>(C, ldc, P.M, bc.v * R, kk, ok, o);
+    store_rows<R, NV, VW>(P, C, ldc, bc.v * R, kk, ok, o);
     acc.zero();
     ++bc.v;
     bc.vb = bc.ve;
@@ -535,7 +545,7 @@ __device__ __forceinline__ void walk_unit(
       acc.store(out);
       settle_rows<R, NV, VW, TB>(P, B, ldb, bc.vb, end, kk, ok, out);
       bc.vb = end;
-      store_rows<R, NV, VW>(C, ldc, P.M, bc.v * R, kk, ok, out);
+      store_rows<R, NV, VW>(P, C, ldc, bc.v * R, kk, ok, out);
       acc.zero();
       ++bc.v;
     }
@@ -569,7 +579,7 @@ __device__ __forceinline__ void finish_unit(
         if (row < P.M) {
 #pragma unroll
           for (int v = 0; v < NV; ++v)
-            if (ok[v]) V::stcs(C + (size_t)row * ldc + kk[v], acc[r][v]);
+            if (ok[v]) put_c<VW>(P.accumulate != 0, C + (size_t)row * ldc + kk[v], acc[r][v]);
         }
       }
     }
@@ -633,7 +643,7 @@ __device__ __forceinline__ void finish_unit(
       if (row < P.M) {
 #pragma unroll
         for (int v = 0; v < NV; ++v)
-          if (ok[v]) V::stcs(C + (size_t)row * ldc + kk[v], acc[r][v]);
+          if (ok[v]) put_c<VW>(P.accumulate != 0, C + (size_t)row * ldc + kk[v], acc[r][v]);
       }
     }
   }
@@ -710,7 +720,7 @@ __global__ void __launch_bounds__(256, (min_blocks_for<R, NV, VW>()))
       walk_unit<R, NV, VW, false>(P, B, ldb, U.y, U.z, kk, ok, 0, 1, sl, L, submask, L,
                                   chunk, bcol, bval, acc, bc, 0, C, ldc);
       settle_rows<R, NV, VW, TB>(P, B, ldb, U.y, U.z, kk, ok, acc);
-      store_rows<R, NV, VW>(C, ldc, P.M, U.x * R, kk, ok, acc);
+      store_rows<R, NV, VW>(P, C, ldc, U.x * R, kk, ok, acc);
     }
   }
 }

@@ -7,7 +7,8 @@ reference's own call sites:
     read_matrix_market_coo   include/mmio.hpp:22      -> vcsr_read_mtx
     coo_to_csr               include/csr.hpp:16       -> vcsr_coo_to_csr
     csr_to_vcsr_spmm         include/vcsr.hpp:25      -> vcsr_build_vcsr (GPU)
-    run_vcsr_spmm_gpu        src/kernels.cu:120       -> vcsr_spmm_segmented
+    run_vcsr_spmm_gpu        src/kernels.cu:120       -> vcsr_plan_from_vcsr +
+                                                       vcsr_spmm_accumulate
     run_csr_spmm_gpu         src/kernels.cu:107       -> vcsr_csr_spmm
     run_cusparse_spmm        src/kernels.cu:170       -> CuSparse
 and Plan (vcsr_plan_*) is the engine's own build-once / run-many operator.
@@ -117,6 +118,10 @@ _SIGS = {
     "vcsr_plan_destroy": (None, [C.c_void_p]),
     "vcsr_spmm": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int,
                             C.c_int, C.c_void_p, C.POINTER(C.c_int)]),
+    "vcsr_spmm_accumulate": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p,
+                                       C.c_int, C.c_int, C.c_void_p, C.POINTER(C.c_int)]),
+    "vcsr_plan_from_vcsr": (C.c_int, [C.POINTER(_Vcsr), C.c_int, C.POINTER(_PlanParams),
+                                      C.POINTER(C.c_void_p), C.c_void_p]),
     "vcsr_spmm_host": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
                                  C.c_void_p]),
     "vcsr_plan_check": (C.c_int, [C.c_void_p, C.c_void_p]),
@@ -421,7 +426,17 @@ def csr_to_vcsr_spmm(dcsr: DeviceCSR, segw=4, bundle=32, stream=None) -> DeviceV
 
 
 def run_vcsr_spmm_gpu(V: DeviceVCSR, dB, O, tileK, dC, stream=None):
-    """run_vcsr_spmm_gpu (src/kernels.cu:120): C += A*B, race-free."""
+    """run_vcsr_spmm_gpu (src/kernels.cu:120): C += A*B for the matrix V
+    holds, on the engine: a plan built on the GPU from V's slots
+    (vcsr_plan_from_vcsr), then vcsr_spmm_accumulate."""
+    plan = Plan.from_vcsr(V, tileK=tileK, max_O=max(O, 512), stream=stream)
+    plan.spmm(dB, dC, O=O, ldb=O, ldc=O, stream=stream, accumulate=True)
+    plan.check(stream)
+
+
+def run_vcsr_spmm_segmented_gpu(V: DeviceVCSR, dB, O, tileK, dC, stream=None):
+    """The segment-major kernel on V itself (vcsr_spmm_segmented): C += A*B,
+    race-free form of src/kernels.cu:37-103."""
     _check(lib().vcsr_spmm_segmented(C.byref(V._s), _ptr(dB), O, tileK, _ptr(dC),
                                      _stream(stream)))
 
@@ -492,6 +507,41 @@ class Plan:
         self.M, self.N, self.nnz = csr.M, csr.N, csr.nnz
         self.last_launches = 0
 
+    @classmethod
+    def from_vcsr(cls, V, tileK=0, max_O=512, stream=None):
+        """The engine's plan for the matrix a segment-major VCSR holds
+        (vcsr_plan_from_vcsr): a DeviceVCSR, or a host VCSRSpMM."""
+        L = lib()
+        p = _PlanParams()
+        L.vcsr_plan_params_default(C.byref(p))
+        p.tileK, p.max_O = tileK, max_O
+        keep = None
+        if isinstance(V, DeviceVCSR):
+            s, where = V._s, DEVICE
+        else:
+            keep = [np.ascontiguousarray(a, dtype) for a, dtype in (
+                (V.group_ptr, np.int32), (V.group_depth, np.int32),
+                (V.group_seg_base, np.int32), (V.group_rows, np.int32),
+                (V.lcol, np.int32), (V.val, np.float32))]
+            s = _Vcsr()
+            s.M, s.N, s.segw, s.bundle = V.M, V.N, V.segw, V.bundle
+            s.num_groups = len(keep[1])
+            s.num_segments = -(-V.N // V.segw) if V.segw > 0 else 0
+            s.num_slots = len(keep[4])
+            (s.group_ptr, s.group_depth, s.group_seg_base, s.group_rows, s.lcol,
+             s.val) = (a.ctypes.data for a in keep)
+            where = HOST
+        p.segw, p.bundle = s.segw, s.bundle
+        h = C.c_void_p()
+        _check(L.vcsr_plan_from_vcsr(C.byref(s), where, C.byref(p), C.byref(h),
+                                     _stream(stream)))
+        self = cls.__new__(cls)
+        self._h = h
+        i = self.info()
+        self.M, self.N, self.nnz = i["M"], i["N"], i["nnz"]
+        self.last_launches = 0
+        return self
+
     def info(self):
         i = _PlanInfo()
         _check(lib().vcsr_plan_get_info(self._h, C.byref(i)))
@@ -502,8 +552,9 @@ class Plan:
         _check(lib().vcsr_plan_export(self._h, C.byref(v)))
         return _vcsr_from_host_struct(v)
 
-    def spmm(self, B, Cout, O=None, ldb=None, ldc=None, stream=None):
-        """C = A*B on device tensors (or raw pointers with O/ldb/ldc given).
+    def spmm(self, B, Cout, O=None, ldb=None, ldc=None, stream=None, accumulate=False):
+        """C = A*B on device tensors (or raw pointers with O/ldb/ldc given);
+        with accumulate=True, C += A*B (vcsr_spmm_accumulate, FP32 B).
         A bfloat16 or float16 B runs vcsr_spmm_bf16 / vcsr_spmm_f16 (FP32 C)."""
         if O is None:
             O = B.shape[1]
@@ -513,7 +564,12 @@ class Plan:
             ldc = Cout.stride(0) if hasattr(Cout, "stride") else O
         n = C.c_int(0)
         dt = str(getattr(B, "dtype", ""))
-        if dt == "torch.bfloat16":  # 16-bit inputs, FP32 sums
+        if accumulate:
+            if dt in ("torch.bfloat16", "torch.float16"):
+                raise VcsrError(5, "accumulate takes an FP32 B")
+            _check(lib().vcsr_spmm_accumulate(self._h, _ptr(B), ldb, _ptr(Cout), ldc, O,
+                                              _stream(stream), C.byref(n)))
+        elif dt == "torch.bfloat16":  # 16-bit inputs, FP32 sums
             _check(lib().vcsr_spmm_bf16(self._h, _ptr(B), ldb, _ptr(Cout), ldc, O,
                                         _stream(stream), C.byref(n)))
         elif dt == "torch.float16":
