@@ -587,9 +587,15 @@ def measure(args, ctx, workload, steps, warmup, extras):
         dt = (time.perf_counter() - t0) / n_e2e
         if world > 1:
             dt = D.max_over_ranks(dist, dt, dev)
+        # rows the call moves (touched B rows up, C rows holding entries
+        # down; the empty C rows are zeroed on the host), over all ranks
+        b_rows, c_rows = plan.host_rows(stream=stream)
+        if world > 1:
+            b_rows = int(D.sum_over_ranks(dist, b_rows, dev))
+            c_rows = int(D.sum_over_ranks(dist, c_rows, dev))
         rec["e2e"] = {"value": round(flops_step / dt / 1e9, 3), "unit": "GFLOP/s",
-                      "h2d_bytes_per_step": int(csr.N * O * 4 * world),
-                      "d2h_bytes_per_step": int(global_M * O * 4),
+                      "h2d_bytes_per_step": int(b_rows * O * 4),
+                      "d2h_bytes_per_step": int(c_rows * O * 4),
                       "ms_per_step": round(dt * 1e3, 4),
                       "api": "vcsr_spmm_host (pinned host B and C)"}
         del hB, hC

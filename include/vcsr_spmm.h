@@ -343,6 +343,21 @@ vcsr_status vcsr_spmm_f16(const vcsr_plan *plan, const void *dB, int ldb,
 vcsr_status vcsr_spmm_host(vcsr_plan *plan, const float *hB, float *hC, int O,
                            vcsr_stream_t stream);
 
+/* Rows vcsr_spmm_host moves across PCIe per call when hB and hC are
+ * page-locked and 64-byte aligned, O is a multiple of 16 and B and C exceed
+ * 8 MB: *b_rows B rows up and *c_rows C rows down.  A product reads only the
+ * B rows of columns that hold an entry, and only the C rows that hold an
+ * entry are non-zero; when these lists save more than 1/8 of B or of C
+ * (graph matrices: R-MAT 2^22 touches 48% of its columns and 52% of its rows
+ * are empty), the entry point moves just those rows (copy kernels reading
+ * and writing the mapped host buffers, up to four column chunks overlapped
+ * as above) and zeroes the empty C rows on host threads; otherwise, and for
+ * plans with tensor-core blocks, *b_rows = N and *c_rows = M.  Builds the row
+ * lists on first use (synchronises `stream`).  No counterpart in the
+ * reference (its main copies all of B and C). */
+vcsr_status vcsr_plan_host_rows(vcsr_plan *plan, int *b_rows, int *c_rows,
+                                vcsr_stream_t stream);
+
 /* Synchronises `stream` and reports a failure that the plan's kernels
  * recorded on the device since the last check (the tensor-core panel kernel
  * bounds every wait on its pipeline barriers and records the first one that

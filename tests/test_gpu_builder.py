@@ -111,5 +111,10 @@ def test_bad_inputs_refused_like_the_host_builder():
 
 def test_full_rmat_gpu_layout_equals_host_layout(tmp_path):
     csr = V.gen_csr("rmat", 0, 22)
-    a = same_layout(tmp_path, csr, max_O=256, target_O=256)
-    assert a.info()["build_ms"] < 1000
+    same_layout(tmp_path, csr, max_O=256, target_O=256)
+    # the build proper, from a CSR already in HBM and with the builder's
+    # kernels loaded: the wall time of a host-CSR build also holds the 522 MB
+    # upload from pageable memory and, in a fresh process, module loading
+    d = V.DeviceCSR(csr)
+    V.Plan(d, max_O=256, target_O=256)
+    assert V.Plan(d, max_O=256, target_O=256).info()["build_ms"] < 500

@@ -5,6 +5,7 @@
 
 #include <atomic>
 #include <cstdint>
+#include <utility>
 #include <vector>
 
 #include "common.h"
@@ -67,6 +68,13 @@ struct vcsr_plan {
   };
   std::vector<RowPanel> rpanels;
   size_t stage_B = 0, stage_C = 0;
+  // rows the host entry point moves with page-locked buffers
+  // (host_transfer.h): touched B rows, C rows holding an entry, and the
+  // ranges [r0, r1) of empty C rows that host threads zero
+  bool xfer_built = false;
+  int *d_xcols = nullptr, *d_xrows = nullptr;
+  int n_xcols = 0, n_xrows = 0;
+  std::vector<std::pair<int, int>> empty_rows;
   double build_ms = 0;
 };
 

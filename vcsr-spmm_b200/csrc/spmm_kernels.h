@@ -53,11 +53,13 @@ LaunchShape pick_shape(int O, int R, bool vec4);
 // `st` with the two events, when there is short work too) and the short-work
 // kernel (on `st`).  side may be null: then both run on `st`.  B holds FP32
 // values, or BF16 ones with bf16 = true (widened to FP32 as they are loaded;
-// not for the plain-CSR rowptr form).
+// not for the plain-CSR rowptr form).  reserve_sms: the grids are sized for
+// that many fewer SMs, so that every block can be resident beside kernels
+// that hold blocks on that many SMs (the host entry point's copy kernels).
 vcsr_status launch_panel_spmm(const PanelDevView &P, bool rowptr,
                               const void *B, int ldb, float *C, int ldc, int O,
                               cudaStream_t st, int *launches, cudaStream_t side,
                               cudaEvent_t fork, cudaEvent_t join,
-                              BType bt = BType::kF32);
+                              BType bt = BType::kF32, int reserve_sms = 0);
 
 }  // namespace vcsr

@@ -30,6 +30,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <mutex>
 #include <utility>
 #include <vector>
@@ -945,13 +946,13 @@ vcsr_status resident_per_sm(const void *fn, int threads, size_t smem, int *per_s
 
 vcsr_status launch_one(KernelFn fn, const PanelDevView &P, long long team_items, int G,
                        const LaunchShape &s, int chunk, size_t smem, const void *B, int ldb,
-                       float *C, int ldc, int O, cudaStream_t st) {
+                       float *C, int ldc, int O, cudaStream_t st, int reserve_sms) {
   const int threads = 256;
   int per_sm = 0;
   VCSR_TRY(resident_per_sm(reinterpret_cast<const void *>(fn), threads, smem, &per_sm));
   const long long items = team_items * s.n_otiles;
   long long blocks = (items + (threads / 32) - 1) / (threads / 32);
-  const long long cap = (long long)sm_count() * per_sm;
+  const long long cap = (long long)std::max(1, sm_count() - reserve_sms) * per_sm;
   blocks = blocks > cap ? cap : (blocks < 1 ? 1 : blocks);
   fn<<<(int)blocks, threads, smem, st>>>(P, B, ldb, C, ldc, O, s.lshift, s.n_otiles, s.W,
                                          chunk);
@@ -964,7 +965,7 @@ vcsr_status launch_one(KernelFn fn, const PanelDevView &P, long long team_items,
 vcsr_status launch_panel_spmm(const PanelDevView &P, bool rowptr, const void *B, int ldb,
                               float *C, int ldc, int O, cudaStream_t st, int *launches,
                               cudaStream_t side, cudaEvent_t fork, cudaEvent_t join,
-                              BType bt) {
+                              BType bt, int reserve_sms) {
   if (launches) *launches = 0;
   const int n_short = rowptr ? P.n_units : P.n_batches;
   const int n_long = rowptr ? 0 : P.n_long;
@@ -990,14 +991,14 @@ vcsr_status launch_panel_spmm(const PanelDevView &P, bool rowptr, const void *B,
     KernelFn fl = select_kernel(P.R, s.NV, s.VW, true, false, bt);
     if (!fl) return fail(VCSR_ERR_UNSUPPORTED, "no kernel for R=%d", P.R);
     VCSR_TRY(launch_one(fl, P, n_long, G, s, chunk, smem, B, ldb, C, ldc, O,
-                        both ? side : st));
+                        both ? side : st, reserve_sms));
     ++n;
   }
   if (n_short > 0) {
     KernelFn fs = select_kernel(P.R, s.NV, s.VW, false, rowptr, bt);
     if (!fs) return fail(VCSR_ERR_UNSUPPORTED, "no kernel for R=%d", P.R);
     VCSR_TRY(launch_one(fs, P, (n_short + G - 1) / G, G, s, chunk, smem, B, ldb, C, ldc, O,
-                        st));
+                        st, reserve_sms));
     ++n;
   }
   if (both) {

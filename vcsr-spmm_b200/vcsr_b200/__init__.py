@@ -125,6 +125,7 @@ _SIGS = {
     "vcsr_spmm_host": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
                                  C.c_void_p]),
     "vcsr_plan_check": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "vcsr_plan_host_rows": (C.c_int, [C.c_void_p, _i32p, _i32p, C.c_void_p]),
     "vcsr_plan_test_withhold_signal": (C.c_int, [C.c_void_p]),
     "vcsr_plan_row_panels": (C.c_int, [C.c_void_p, C.POINTER(C.c_int), C.c_void_p,
                                        C.c_void_p, C.c_void_p]),
@@ -638,6 +639,14 @@ class Plan:
         O = hB.shape[1] if hB is not None else hC.shape[1]
         _check(lib().vcsr_spmm_host(self._h, _ptr(hB), _ptr(hC), O, _stream(stream)))
         return hC
+
+    def host_rows(self, stream=None):
+        """(B rows up, C rows down) per spmm_host call with page-locked
+        buffers, O a multiple of 16 and more than 8 MB of B and C."""
+        b, c = np.zeros(1, np.int32), np.zeros(1, np.int32)
+        _check(lib().vcsr_plan_host_rows(self._h, b.ctypes.data_as(_i32p),
+                                         c.ctypes.data_as(_i32p), _stream(stream)))
+        return int(b[0]), int(c[0])
 
     def close(self):
         if getattr(self, "_h", None) and _LIB is not None:
