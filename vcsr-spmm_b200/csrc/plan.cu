@@ -568,7 +568,20 @@ vcsr_status spmm_impl(const vcsr_plan *p, const float *dB, int ldb, float *dC, i
     if (launches) *launches = n1 + n2;
     return VCSR_OK;
   }
-  VCSR_TRY(vcsr::launch_panel_spmm(pv, false, dB, ldb, dC, ldc, O, (cudaStream_t)stream,
+  // Single-row vectors with no long or split rows and at least 8 entries per
+  // row on average (uniform-degree matrices): one sub-warp per row, straight
+  // from the row offsets (vec_ptr is the CSR's row_ptr when R = 1), one
+  // dependent load fewer than a batch record and its vector offsets.
+  // Measured on B200, uniform 16 entries per row at O = 32: 4,096 rows
+  // 10.1 -> 8.3 us, 65,536 rows 28.6 -> 25.6 us, 2^20 rows 462 -> 436 us;
+  // O = 128 unchanged; the sums are the same (each row in CSR order).
+  const bool by_rows = p->R == 1 && p->n_long == 0 && p->n_split_units == 0 &&
+                       p->n_panel_rb == 0 && p->num_union >= 8LL * p->M;
+  if (by_rows) {
+    pv.row_ptr = p->d_vec_ptr;
+    pv.n_units = p->M;
+  }
+  VCSR_TRY(vcsr::launch_panel_spmm(pv, by_rows, dB, ldb, dC, ldc, O, (cudaStream_t)stream,
                                    &n1, p->side, p->fork, p->join));
   if (p->n_panel_rb > 0) {  // C += dense panels * B on the tensor cores
     vcsr::TcView tv;
