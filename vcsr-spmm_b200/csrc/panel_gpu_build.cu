@@ -719,6 +719,38 @@ vcsr_status choose_vec_rows_device(const vcsr_csr &w, int sms, Scratch &sc, int 
 
 }  // namespace
 
+__global__ void long_first_col_kernel(const int4 *__restrict__ units,
+                                      const int *__restrict__ lidx,
+                                      const int *__restrict__ ucol, int n, uint32_t *keys,
+                                      int *vals) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const int u = lidx[i];
+    keys[i] = (uint32_t)ucol[units[u].y];
+    vals[i] = u;
+  }
+}
+
+vcsr_status order_long_by_column(vcsr_plan *p, cudaStream_t st) {
+  const int n = p->n_long;
+  if (n <= 1 || p->d_long_col) return VCSR_OK;
+  Scratch sc(st);
+  uint32_t *kin = nullptr, *kout = nullptr;
+  int *vin = nullptr;
+  VCSR_TRY(sc.get(&kin, n));
+  VCSR_TRY(sc.get(&kout, n));
+  VCSR_TRY(sc.get(&vin, n));
+  VCSR_TRY(dmalloc(&p->d_long_col, n));
+  long_first_col_kernel<<<grid_for(n), kThreads, 0, st>>>(p->d_units, p->d_long, p->d_ucol, n,
+                                                          kin, vin);
+  VCSR_CUDA(cudaGetLastError());
+  int bits = 1;
+  while (bits < 32 && (1LL << bits) < (long long)p->N) ++bits;
+  VCSR_TRY(radix_sort_pairs(kin, vin, kout, p->d_long_col, n, bits, sc));
+  acct(p, 4, n);
+  VCSR_CUDA(cudaStreamSynchronize(st));  // the scratch dies here
+  return VCSR_OK;
+}
+
 vcsr_status build_plan_layout_device(vcsr_plan *p, const vcsr_csr &d, int sms,
                                      cudaStream_t st) {
   const vcsr_plan_params &params = p->params;

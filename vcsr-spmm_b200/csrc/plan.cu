@@ -32,7 +32,8 @@ namespace vcsr {
 
 void plan_release(vcsr_plan *p) {
   cudaFree(p->d_ucol); cudaFree(p->d_uval); cudaFree(p->d_umask); cudaFree(p->d_units);
-  cudaFree(p->d_batches); cudaFree(p->d_long); cudaFree(p->d_vec_ptr);
+  cudaFree(p->d_batches); cudaFree(p->d_long); cudaFree(p->d_long_col);
+  cudaFree(p->d_vec_ptr);
   cudaFree(p->d_parts); cudaFree(p->d_svecs); cudaFree(p->d_partials);
   cudaFree(p->d_counters); cudaFree(p->d_stage_B); cudaFree(p->d_stage_C);
   cudaFree(p->d_xcols); cudaFree(p->d_xrows);
@@ -50,6 +51,7 @@ void plan_release(vcsr_plan *p) {
 }
 
 vcsr_status plan_finish(vcsr_plan *p, cudaStream_t st) {
+  VCSR_TRY(order_long_by_column(p, st));
   if (p->n_long > 0 && p->n_batches > 0) {
     cudaError_t e = cudaStreamCreateWithFlags(&p->side, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->fork, cudaEventDisableTiming);
@@ -93,6 +95,13 @@ vcsr::PanelDevView view(const vcsr_plan *p) {
   v.n_split_units = p->n_split_units;
   v.M = p->M;
   v.R = p->R;
+  return v;
+}
+
+// The view for a launch over the whole matrix: long units in column order.
+vcsr::PanelDevView view_all(const vcsr_plan *p) {
+  vcsr::PanelDevView v = view(p);
+  if (p->d_long_col) v.long_idx = p->d_long_col;
   return v;
 }
 
@@ -546,7 +555,7 @@ vcsr_status spmm_impl(const vcsr_plan *p, const float *dB, int ldb, float *dC, i
                 "O=%d exceeds the plan's max_O=%d (split rows need scratch)", O,
                 p->pstride);
   int n1 = 0, n2 = 0;
-  vcsr::PanelDevView pv = view(p);
+  vcsr::PanelDevView pv = view_all(p);
   pv.accumulate = accumulate ? 1 : 0;
   if (p->n_seg_rb > 0) {  // tensor-core segments; the residual (if any) first
     if (!p->seg_only)
@@ -672,7 +681,7 @@ vcsr_status spmm_16bit(const vcsr_plan *p, const void *dB, int ldb, float *dC, i
   if (p->n_split_units > 0 && O > p->pstride)
     return fail(VCSR_ERR_INVALID,
                 "O=%d exceeds the plan's max_O=%d (split rows need scratch)", O, p->pstride);
-  return vcsr::launch_panel_spmm(view(p), false, dB, ldb, dC, ldc, O, (cudaStream_t)stream,
+  return vcsr::launch_panel_spmm(view_all(p), false, dB, ldb, dC, ldc, O, (cudaStream_t)stream,
                                  launches, p->side, p->fork, p->join, bt);
 }
 
@@ -791,7 +800,7 @@ vcsr_status host_rows_pipeline(vcsr_plan *p, const float *hB, float *hC, int O,
       status = fail(VCSR_ERR_CUDA, "chunk wait: %s", cudaGetErrorString(e));
       break;
     }
-    status = vcsr::launch_panel_spmm(view(p), false, p->d_stage_B + o0, O, p->d_stage_C + o0, O,
+    status = vcsr::launch_panel_spmm(view_all(p), false, p->d_stage_B + o0, O, p->d_stage_C + o0, O,
                                      w, p->comp, nullptr, p->side, p->fork, p->join,
                                      vcsr::BType::kF32, reserve);
     if (status != VCSR_OK) break;

@@ -27,6 +27,9 @@ struct vcsr_plan {
   int4 *d_batches = nullptr;
   int *d_long = nullptr, *d_vec_ptr = nullptr;
   int n_batches = 0, n_long = 0;
+  // the long units ordered by their first union column (launches over the
+  // whole matrix; d_long keeps vector order for the row panels)
+  int *d_long_col = nullptr;
   int2 *d_parts = nullptr;
   int2 *d_svecs = nullptr;
   float *d_partials = nullptr;
