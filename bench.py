@@ -582,7 +582,8 @@ def measure(args, ctx, workload, steps, warmup, extras):
     # end to end through the host-buffer entry point (pinned buffers)
     if extras and not args.no_e2e and not half:  # the host-buffer entry point takes FP32 B
         hB = torch.empty(csr.N, O, dtype=torch.float32, pin_memory=True)
-        hB.copy_(dB32.cpu())
+        hB.copy_(dB32)  # device to pinned host, no pageable copy of B on the way
+        torch.cuda.synchronize()
         hC = torch.empty(csr.M, O, dtype=torch.float32, pin_memory=True)
         for _ in range(max(3, min(5, warmup))):
             plan.spmm_host(hB.numpy(), hC.numpy(), stream=stream)
