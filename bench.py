@@ -18,7 +18,8 @@ Other workloads (`--workload`; synthetic stand-ins with the benchmark
 configurations' shapes):
   fem            62,451 x 62,451 FEM-style banded, ~4.0M nnz, O = 128.  With
                  N GPUs every rank owns one such panel: weak scaling.
-  fem_o32 / fem_o512, uniform (O=32), powerlaw_o8 / powerlaw_o64,
+  fem_o32 / fem_o512, uniform (O=32), powerlaw_o8 / powerlaw_o64 /
+  powerlaw_o128,
   blockdense (O=512): single-panel variants (weak scaling under N GPUs).
   blockdense_tf32  the same matrix with its dense 16x16 blocks on the
                  tensor cores in TF32 (VCSR_PLAN_TF32_PANELS).
@@ -54,6 +55,9 @@ WORKLOADS = {
     "uniform": ("uniform", 0, 32, "weak", "uniform_4096_16pr_O32"),
     "powerlaw_o8": ("powerlaw", 0, 8, "weak", "powerlaw_321821_O8"),
     "powerlaw_o64": ("powerlaw", 0, 64, "weak", "powerlaw_321821_O64"),
+    # the north star states its roofline and cuSPARSE targets for the
+    # power-law matrix at O = 128
+    "powerlaw_o128": ("powerlaw", 0, 128, "weak", "powerlaw_321821_O128"),
     "blockdense": ("blockdense", 0, 512, "weak", "blockdense_65536_O512_fp32"),
     "blockdense_tf32": ("blockdense", 0, 512, "weak", "blockdense_65536_O512_tf32"),
     "rmat_bf16": ("rmat", 22, 256, "strong", "rmat_s22_O256_bf16in"),
