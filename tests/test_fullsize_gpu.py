@@ -46,7 +46,7 @@ def csr_order(plan, O):
 
 
 @pytest.mark.parametrize("cfg,O", [("fem", 32), ("fem", 512), ("powerlaw", 8),
-                                   ("powerlaw", 64), ("uniform", 32)])
+                                   ("powerlaw", 64), ("powerlaw", 128), ("uniform", 32)])
 def test_full_size_elementwise(cfg, O):
     csr = V.gen_csr(cfg, 0)
     plan = bench_plan(csr, O)
